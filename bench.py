@@ -1,0 +1,455 @@
+"""bench.py -- CVSA decode step on B200 (one JSON line from rank 0).
+
+Workload (N=1): BASELINE config 2 -- Llama-3.1-8B attention geometry, B=32
+sequences of 8192 tokens (512 pages of 16), Hq=32, Hkv=8, D=128, bf16 paged
+KV with a permuted page table, budget 5 % (25 pages) + 3 forced pages,
+tau=0.9, lazy schedule M=4 (page scoring + coverage gate every 4 steps,
+selection reuse between), over 32 layers with 32 independent KV pools
+(1.07 GB of K+V each, so every layer's inputs exceed the 126 MB L2).
+Synthetic seeded data (no checkpoints, no datasets).
+
+A step is one decode step through all 32 layers (`CVSABackend.__call__` per
+layer, i.e. one cvsa_decode_step C-ABI call per layer). The metric is the
+achieved HBM bandwidth on the KV bytes the CVSA algorithm reads (whole job,
+GB/s): scoring steps read every valid page's K, every step reads the selected
+pages' K+V, and recovery reads the complement pages' K+V of rejected heads;
+the per-layer step time (us/layer) is reported beside it.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl cvsa|reference]
+
+--impl reference times the reference's algorithm on the host cores: the
+pure-PyTorch restatement in oracle/cvsa_ref.py (the reference itself is
+Triton + PyTorch and cannot run without its GPU kernels), on a bounded sample
+of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "coverage-verified-sparse-attention_b200")
+for _p in (PKG, ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+M_INTERVAL = 4
+LAYERS = 32
+KP_BYTES = 16 * 128 * 2        # one K (or V) page of one KV head, bf16
+METRIC = "CVSA decode-step achieved HBM GB/s on algorithmic KV bytes (config 2, 8K ctx)"
+WORKLOAD = ("config2: Llama-3.1-8B attention, B=32, Hq=32, Hkv=8, D=128, bf16, ctx=8192 "
+            "(512 pages x 16), budget 5% (25) + sink 1 + local 2, tau=0.9, lazy M=4, "
+            "32 layers with independent pools")
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    return ws, rank, local
+
+
+def _barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def _max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _sum_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def _scoring_pages(context_lens, hkv):
+    nv = (context_lens.to(torch.int64) + 15) // 16
+    return int(nv.sum()) * hkv
+
+
+# ----------------------------------------------------------------------------
+# reference (CPU) arm
+# ----------------------------------------------------------------------------
+
+class CpuSample:
+    """The oracle restatement of the reference path, timed on the host cores.
+
+    Sample: one layer of config 2 (all 32 sequences, 8K context) under the
+    lazy M=4 schedule, in the reference's fp32 arithmetic, with every host
+    thread. A CPU "step" is one M=4 cycle (lazy check step + 3 reuse steps).
+    """
+
+    def __init__(self, threads: int = None):
+        from cvsa import synthetic
+        from oracle import cvsa_ref as R
+
+        self.threads = threads or os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.wl = synthetic.config2(device="cpu", seed=123)
+        wl = self.wl
+        self.be = R.OracleBackend(8, 32, 128, 16, num_layers=1, budget_pct=wl.budget_pct,
+                                  coverage_threshold=wl.tau, lazy=True,
+                                  check_interval=M_INTERVAL, sink_pages=1, local_pages=2,
+                                  precise=False)
+
+    def cycle(self):
+        """Run one M=4 cycle; returns (seconds, algorithmic KV bytes)."""
+        wl, be = self.wl, self.be
+        w0, lazy0 = be.attn_work, be.total_coverage_checks
+        t0 = time.perf_counter()
+        for _ in range(M_INTERVAL):
+            be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+            be.step_done(0, 1)
+        dt = time.perf_counter() - t0
+        pages = be.attn_work - w0
+        lazy = be.total_coverage_checks - lazy0
+        nbytes = pages * 2 * KP_BYTES + lazy * _scoring_pages(wl.context_lens, 8) * KP_BYTES
+        return dt, nbytes
+
+
+CPU_SAMPLE_DESC = ("one layer of config 2 (all 32 sequences, 8K ctx) under the lazy M=4 schedule, "
+                   "one M=4 cycle (lazy check + 3 reuse steps) per step, fp32 torch restatement "
+                   "of the reference on CPU")
+
+
+def run_reference(args, ws, rank):
+    if rank != 0:
+        return
+    cs = CpuSample()
+    threads = cs.threads
+    for _ in range(args.warmup):
+        cs.cycle()
+    tot_t, tot_b = 0.0, 0
+    for _ in range(args.steps):
+        dt, nb = cs.cycle()
+        tot_t += dt
+        tot_b += nb
+    value = tot_b / tot_t / 1e9
+    sample = CPU_SAMPLE_DESC
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": tot_t / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------
+# CUDA arm
+# ----------------------------------------------------------------------------
+
+def build_layers(dev, layers):
+    from cvsa import synthetic
+    wls = []
+    for l in range(layers):
+        wls.append(synthetic.config2(device=dev, seed=1000 + l, gen_device=str(dev)))
+    torch.cuda.synchronize()
+    return wls
+
+
+def run_cvsa(args, ws, rank, local):
+    from cvsa import _lib
+    from cvsa.backend import CVSABackend
+
+    dev = torch.device("cuda", local)
+    layers = args.layers
+    wls = build_layers(dev, layers)
+    B, Hq, D = wls[0].q.shape
+    hkv = wls[0].num_kv_heads
+
+    def make_backend():
+        return CVSABackend(hkv, Hq, D, 16, num_layers=layers, budget_pct=0.05,
+                           coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
+                           sink_pages=1, local_pages=2)
+
+    def step(be, qs=None, outs=None):
+        for l, wl in enumerate(wls):
+            q = wl.q if qs is None else qs[l]
+            o = be(q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+            if outs is not None:
+                outs[l] = o
+            be.step_done(l, layers)
+
+    def timed(be, k, fn):
+        _barrier(ws)
+        torch.cuda.synchronize()
+        c0 = be._counter_values()
+        lazy_steps = sum(1 for s in range(be._step, be._step + k) if s % M_INTERVAL == 0)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(k):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        ms = e0.elapsed_time(e1)
+        c1 = be._counter_values()
+        pages = c1[_lib.CTR_PAGES_ATTENDED] - c0[_lib.CTR_PAGES_ATTENDED]
+        nbytes = pages * 2 * KP_BYTES + lazy_steps * sum(
+            _scoring_pages(wl.context_lens, hkv) for wl in wls) * KP_BYTES
+        return ms, nbytes, lazy_steps
+
+    # ---- device-resident timing (value) ----
+    be = make_backend()
+    warm = args.warmup + ((-args.warmup) % M_INTERVAL)   # timed region starts a cycle
+    for _ in range(warm):
+        step(be)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ms, nbytes, lazy_steps = timed(be, args.steps, lambda: step(be))
+    clk = clocks.stop()
+    ms_max = _max_over_ranks(ms, ws)
+    bytes_all = _sum_over_ranks(float(nbytes), ws)
+    value = bytes_all / (ms_max * 1e-3) / 1e9
+    us_per_layer = ms_max * 1e3 / (args.steps * layers)
+    launches = (lazy_steps * 3 + (args.steps - lazy_steps) * 1) * layers
+    stats = be.get_stats()
+
+    # ---- per-kernel timing pass (events around each launch, same K steps) ----
+    ev_sets = {}
+
+    def step_events(be2):
+        for l, wl in enumerate(wls):
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NUM_EVENTS)]
+            arr = (__import__("ctypes").c_void_p * _lib.NUM_EVENTS)(
+                *[e.cuda_event for e in evs])
+            be2._timing_events = arr
+            be2(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+            be2._timing_events = None
+            ev_sets.setdefault(be2._step, []).append((evs, arr))
+            be2.step_done(l, layers)
+
+    be2 = make_backend()
+    for _ in range(warm):
+        step(be2)
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        step_events(be2)
+    torch.cuda.synchronize()
+    kern = {"score": [], "select": [], "attend_scoring": [], "attend_reuse": []}
+    for s, lst in ev_sets.items():
+        for evs, _ in lst:
+            e = evs
+            try:
+                kern["score"].append(e[_lib.EV_SCORE_BEGIN].elapsed_time(e[_lib.EV_SCORE_END]))
+                kern["select"].append(e[_lib.EV_SELECT_BEGIN].elapsed_time(e[_lib.EV_SELECT_END]))
+                kern["attend_scoring"].append(
+                    e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END]))
+            except RuntimeError:
+                kern["attend_reuse"].append(
+                    e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END]))
+    score_ms = statistics.mean(kern["score"]) if kern["score"] else None
+    score_bytes = _scoring_pages(wls[0].context_lens, hkv) * KP_BYTES
+    peak, peak_kind = _peaks()
+    achieved = score_bytes / (score_ms * 1e-3) / 1e9 if score_ms else None
+    traffic = None
+    tfile = os.path.join(ROOT, "profiles", "score_pages_config2_traffic.json")
+    if os.path.exists(tfile):
+        with open(tfile) as f:
+            traffic = json.load(f).get("bytes_per_launch")
+    reuse_ms = statistics.mean(kern["attend_reuse"]) if kern["attend_reuse"] else None
+    sel_pages = B * hkv * 28
+    reuse_bytes = sel_pages * 2 * KP_BYTES
+
+    # ---- end-to-end through the public API with host buffers ----
+    be3 = make_backend()
+    q_host = [wl.q.cpu().pin_memory() for wl in wls]
+    out_host = [torch.empty_like(h).pin_memory() for h in q_host]
+    q_dev = [torch.empty_like(wl.q) for wl in wls]
+
+    def e2e_step():
+        for l, wl in enumerate(wls):
+            q_dev[l].copy_(q_host[l], non_blocking=True)
+            o = be3(q_dev[l], wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+            out_host[l].copy_(o, non_blocking=True)
+            be3.step_done(l, layers)
+
+    for _ in range(warm):
+        e2e_step()
+    torch.cuda.synchronize()
+    ms_e, nbytes_e, _ = timed(be3, args.steps, e2e_step)
+    ms_e = _max_over_ranks(ms_e, ws)
+    e2e_val = _sum_over_ranks(float(nbytes_e), ws) / (ms_e * 1e-3) / 1e9
+    h2d = sum(h.numel() * h.element_size() for h in q_host)
+
+    # ---- CPU baseline (rank 0, N=1 only) ----
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        cs = CpuSample()
+        cs.cycle()                       # warm-up cycle (first step has no cache)
+        tot_t, tot_b, cycles = 0.0, 0, 0
+        while tot_t < 10.0:
+            dt, nb = cs.cycle()
+            tot_t += dt
+            tot_b += nb
+            cycles += 1
+        cpu = {"value": tot_b / tot_t / 1e9, "unit": "GB/s", "cores": cs.threads,
+               "kind": "port", "sample": CPU_SAMPLE_DESC + f"; {cycles} cycles, {tot_t:.1f} s",
+               "ms_per_layer_step": tot_t * 1e3 / (M_INTERVAL * cycles)}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": warm, "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) + planted heavy pages; no checkpoints)",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "ctx": 8192, "layers": layers,
+                       "schedule": f"lazy M={M_INTERVAL}",
+                       "l2": "inputs larger than L2 (1.07 GB K+V per layer, 32 pools)",
+                       "parallelism": f"{ws} independent replicas (weak scaling)"},
+            "us_per_layer": us_per_layer,
+            "tokens_per_s": B * ws * args.steps / (ms_max * 1e-3),
+            "roofline": {"bound": "hbm", "kernel": "score_pages_kernel",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": (achieved / peak) if achieved else None,
+                         "traffic": traffic, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": score_bytes,
+                         "avg_launch_ms": score_ms},
+            "kernels": {
+                "score_ms": score_ms,
+                "select_ms": statistics.mean(kern["select"]) if kern["select"] else None,
+                "attend_scoring_ms": (statistics.mean(kern["attend_scoring"])
+                                      if kern["attend_scoring"] else None),
+                "attend_reuse_ms": reuse_ms,
+                "attend_reuse_gbs": reuse_bytes / (reuse_ms * 1e-3) / 1e9 if reuse_ms else None,
+            },
+            "cvsa_stats": {k: stats[k] for k in ("per_head_accept_rate", "effective_budget_pct",
+                                                 "total_scoring_steps", "total_coverage_checks")
+                           if k in stats},
+            "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": h2d, "ms_per_step": ms_e / args.steps},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--impl", default="cvsa", choices=["cvsa", "reference"])
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        ws = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, ws, rank)
+        return
+    ws, rank, local = _dist()
+    try:
+        run_cvsa(args, ws, rank, local)
+    finally:
+        if ws > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

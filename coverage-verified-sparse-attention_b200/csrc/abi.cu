@@ -1,0 +1,571 @@
+// extern "C" entry points of libcvsa_b200.so (declared in include/cvsa_b200.h).
+//
+// This layer validates arguments (returning the status codes the Python
+// shims map to the reference's exceptions), carves caller-provided
+// workspaces, and sequences the kernels of one CVSA layer step on the
+// caller's stream. It never allocates device memory and never synchronises.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "cvsa_internal.h"
+
+namespace cvsa {
+
+int dtype_bytes(int dtype) {
+  switch (dtype) {
+    case CVSA_DTYPE_F32: return 4;
+    case CVSA_DTYPE_F16: return 2;
+    case CVSA_DTYPE_BF16: return 2;
+    default: return 0;
+  }
+}
+
+int num_sms() {
+  static int cache[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+    n = 148;
+  if (dev >= 0 && dev < 64) cache[dev] = n;
+  return n;
+}
+
+}  // namespace cvsa
+
+using namespace cvsa;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return CVSA_OK;
+  return fail(CVSA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool valid_dtype(int dt) { return dt == CVSA_DTYPE_F32 || dt == CVSA_DTYPE_F16 || dt == CVSA_DTYPE_BF16; }
+
+int check_kv(const cvsa_kv_desc_t* kv, KvView* out) {
+  if (!kv) return fail(CVSA_ERR_INVALID, "kv descriptor is NULL");
+  if (!kv->k_cache || !kv->v_cache) return fail(CVSA_ERR_INVALID, "k_cache/v_cache is NULL");
+  if (!valid_dtype(kv->dtype)) return fail(CVSA_ERR_INVALID, "kv dtype %d unknown", kv->dtype);
+  if (kv->num_blocks <= 0 || kv->block_size <= 0 || kv->num_kv_heads <= 0 || kv->head_dim <= 0)
+    return fail(CVSA_ERR_INVALID, "kv shape must be positive (blocks=%d bs=%d hkv=%d d=%d)",
+                kv->num_blocks, kv->block_size, kv->num_kv_heads, kv->head_dim);
+  const int eb = dtype_bytes(kv->dtype);
+  if (kv->stride_head < kv->head_dim || kv->stride_token < 1 || kv->stride_block < 1)
+    return fail(CVSA_ERR_INVALID, "kv strides inconsistent with head_dim");
+  if ((reinterpret_cast<uintptr_t>(kv->k_cache) | reinterpret_cast<uintptr_t>(kv->v_cache)) % 16 ||
+      (kv->stride_head * eb) % 16 || (kv->stride_token * eb) % 16 ||
+      (kv->stride_block * eb) % 16 || (kv->head_dim * eb) % 16)
+    return fail(CVSA_ERR_INVALID, "kv rows must be 16-byte aligned");
+  out->k = kv->k_cache;
+  out->v = kv->v_cache;
+  out->dtype = kv->dtype;
+  out->num_blocks = kv->num_blocks;
+  out->bs = kv->block_size;
+  out->hkv = kv->num_kv_heads;
+  out->d = kv->head_dim;
+  out->sb = kv->stride_block;
+  out->st = kv->stride_token;
+  out->sh = kv->stride_head;
+  return CVSA_OK;
+}
+
+int check_q(const cvsa_query_desc_t* qd, const KvView& kv, bool need_q, QView* out) {
+  if (!qd) return fail(CVSA_ERR_INVALID, "query descriptor is NULL");
+  if (need_q && !qd->q) return fail(CVSA_ERR_INVALID, "q is NULL");
+  if (!valid_dtype(qd->dtype)) return fail(CVSA_ERR_INVALID, "q dtype %d unknown", qd->dtype);
+  if (qd->batch < 0) return fail(CVSA_ERR_INVALID, "batch < 0");
+  if (qd->num_q_heads <= 0 || qd->num_q_heads % kv.hkv != 0)
+    return fail(CVSA_ERR_INVALID, "num_q_heads=%d is not a positive multiple of num_kv_heads=%d",
+                qd->num_q_heads, kv.hkv);
+  if (qd->max_pages <= 0) return fail(CVSA_ERR_INVALID, "max_pages must be positive");
+  if (qd->batch > 0 && (!qd->block_tables || !qd->context_lens))
+    return fail(CVSA_ERR_INVALID, "block_tables/context_lens is NULL");
+  if (need_q && (reinterpret_cast<uintptr_t>(qd->q) % 16))
+    return fail(CVSA_ERR_INVALID, "q must be 16-byte aligned");
+  out->q = qd->q;
+  out->dtype = qd->dtype;
+  out->B = qd->batch;
+  out->hq = qd->num_q_heads;
+  out->W = qd->max_pages;
+  out->tables = qd->block_tables;
+  out->lens = qd->context_lens;
+  return CVSA_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+// Largest page count the select kernel can hold in shared memory.
+constexpr int kMaxPagesSelect = 40000;
+
+int bitmap_words(int W) { return (W + 31) / 32; }
+
+size_t decode_ws(const QView& q, const KvView& kv, int max_sel) {
+  size_t a = attend_workspace_bytes(q, kv, max_sel, false, false);
+  size_t b = attend_workspace_bytes(q, kv, max_sel, true, false);
+  size_t bm = align256((size_t)q.B * kv.hkv * bitmap_words(q.W) * 4);
+  return (a > b ? a : b) + bm;
+}
+
+struct StepLayout {
+  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, sync, attend, total;
+};
+
+StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense) {
+  StepLayout L;
+  const size_t bh = (size_t)q.B * kv.hkv;
+  size_t off = 0;
+  L.scores = off; off += align256(bh * q.W * 4);
+  L.sel = off; off += align256(bh * max_sel * 4);
+  L.n = off; off += align256(bh * 4);
+  L.bitmap = off; off += align256(bh * bitmap_words(q.W) * 4);
+  L.acc_new = off; off += align256(bh);
+  L.cov_new = off; off += align256(bh * 4);
+  L.acc_c = off; off += align256(bh);
+  L.cov_c = off; off += align256(bh * 4);
+  L.sync = off; off += 256;
+  L.attend = off; off += attend_workspace_bytes(q, kv, max_sel, recover, dense);
+  L.total = off;
+  return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cvsa_abi_version(void) { return CVSA_ABI_VERSION; }
+
+const char* cvsa_status_string(int status) {
+  switch (status) {
+    case CVSA_OK: return "ok";
+    case CVSA_ERR_INVALID: return "invalid argument";
+    case CVSA_ERR_UNSUPPORTED: return "unsupported shape or dtype";
+    case CVSA_ERR_WORKSPACE: return "workspace too small or misaligned";
+    case CVSA_ERR_CUDA: return "CUDA error";
+    case CVSA_ERR_POOL: return "page pool exhausted";
+    default: return "unknown status";
+  }
+}
+
+const char* cvsa_last_error(void) { return g_last_error.c_str(); }
+
+int cvsa_score_pages(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd, float* page_scores,
+                     void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (!page_scores) return fail(CVSA_ERR_INVALID, "page_scores is NULL");
+  if (!score_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "scoring built for block_size 16, head_dim 64/128/256");
+  if (q.B == 0) return CVSA_OK;
+  return cuda_status(launch_score_pages(q, kv, page_scores, nullptr, (cudaStream_t)stream, false),
+                     "score_pages launch");
+}
+
+int cvsa_select_pages(const float* page_scores, int32_t batch, int32_t num_kv_heads,
+                      int32_t max_pages, const int32_t* context_lens, int32_t block_size,
+                      int32_t budget, int32_t sink_pages, int32_t local_pages,
+                      int32_t* page_indices, int32_t max_sel, int32_t* n_per_head,
+                      void* stream) {
+  if (batch < 0 || num_kv_heads <= 0 || max_pages <= 0 || block_size <= 0)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if (budget < 0 || sink_pages < 0 || local_pages < 0)
+    return fail(CVSA_ERR_INVALID, "budget/sink/local must be >= 0");
+  if (max_sel < budget + sink_pages + local_pages || max_sel <= 0)
+    return fail(CVSA_ERR_INVALID, "max_sel=%d < budget+sink+local=%d", max_sel,
+                budget + sink_pages + local_pages);
+  if (max_pages > kMaxPagesSelect)
+    return fail(CVSA_ERR_UNSUPPORTED, "max_pages=%d above %d", max_pages, kMaxPagesSelect);
+  if (batch == 0) return CVSA_OK;
+  if (!page_scores || !context_lens || !page_indices || !n_per_head)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  SelectParams p;
+  memset(&p, 0, sizeof(p));
+  p.scores = page_scores;
+  p.B = batch;
+  p.hkv = num_kv_heads;
+  p.W = max_pages;
+  p.bs = block_size;
+  p.lens = context_lens;
+  p.budget = budget;
+  p.sink = sink_pages;
+  p.local = local_pages;
+  p.tau = 0.f;
+  p.sel_idx = page_indices;
+  p.sel_n = n_per_head;
+  p.max_sel = max_sel;
+  p.mode = -1;
+  return cuda_status(launch_select_gate(p, (cudaStream_t)stream, false), "select launch");
+}
+
+int cvsa_check_coverage(const float* page_scores, int32_t batch, int32_t num_kv_heads,
+                        int32_t max_pages, const int32_t* page_indices, int32_t max_sel,
+                        const int32_t* n_per_head, float tau, uint8_t* accept, float* coverage,
+                        void* stream) {
+  if (batch < 0 || num_kv_heads <= 0 || max_pages <= 0 || max_sel <= 0)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if (max_pages > kMaxPagesSelect)
+    return fail(CVSA_ERR_UNSUPPORTED, "max_pages=%d above %d", max_pages, kMaxPagesSelect);
+  if (batch == 0) return CVSA_OK;
+  if (!page_scores || !page_indices || !n_per_head || !accept)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  return cuda_status(launch_check_coverage(page_scores, batch, num_kv_heads, max_pages,
+                                           page_indices, max_sel, n_per_head, tau, accept,
+                                           coverage, (cudaStream_t)stream),
+                     "coverage launch");
+}
+
+int cvsa_compute_complement(const int32_t* page_indices, int32_t max_sel,
+                            const int32_t* n_per_head, const int32_t* context_lens, int32_t batch,
+                            int32_t num_kv_heads, int32_t block_size, const uint8_t* accept,
+                            int32_t* complement, int32_t max_comp, int32_t* n_complement,
+                            void* stream) {
+  if (batch < 0 || num_kv_heads <= 0 || block_size <= 0 || max_sel <= 0 || max_comp <= 0)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if ((int64_t)max_comp + max_sel > 200000)
+    return fail(CVSA_ERR_UNSUPPORTED, "max_comp + max_sel above 200000");
+  if (batch == 0) return CVSA_OK;
+  if (!page_indices || !n_per_head || !context_lens || !complement || !n_complement)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  return cuda_status(launch_complement(page_indices, max_sel, n_per_head, context_lens, batch,
+                                       num_kv_heads, block_size, accept, complement, max_comp,
+                                       n_complement, (cudaStream_t)stream),
+                     "complement launch");
+}
+
+size_t cvsa_decode_workspace_size(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
+                                  int32_t max_sel) {
+  KvView kv;
+  QView q;
+  if (check_kv(kvd, &kv) || check_q(qd, kv, false, &q) || max_sel <= 0) return 0;
+  return decode_ws(q, kv, max_sel);
+}
+
+int cvsa_sparse_decode(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
+                       const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
+                       float* o_unnorm, float* m, float* l, void* out, int32_t out_dtype,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (max_sel <= 0) return fail(CVSA_ERR_INVALID, "max_sel must be positive");
+  if (!attend_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "decode built for block_size 16, head_dim 64/128/256, G<=16");
+  if (out && !valid_dtype(out_dtype)) return fail(CVSA_ERR_INVALID, "out dtype unknown");
+  if (!out && !o_unnorm && !m && !l) return fail(CVSA_ERR_INVALID, "no output requested");
+  if (q.B == 0) return CVSA_OK;
+  if (!page_indices || !n_per_head) return fail(CVSA_ERR_INVALID, "NULL selection");
+  const size_t need = decode_ws(q, kv, max_sel);
+  if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(CVSA_ERR_WORKSPACE, "workspace needs %zu bytes, 256-aligned", need);
+  AttendParams p;
+  memset(&p, 0, sizeof(p));
+  p.sel0 = page_indices;
+  p.n0 = n_per_head;
+  p.sel_stride = max_sel;
+  p.src_select = 0;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.o_unnorm = o_unnorm;
+  p.m_out = m;
+  p.l_out = l;
+  p.workspace = workspace;
+  p.ws_bytes = workspace_bytes;
+  return cuda_status(launch_attend(q, kv, p, max_sel, (cudaStream_t)stream, false),
+                     "decode launch");
+}
+
+int cvsa_lse_merge(const float* o_d, const float* m_d, const float* l_d, const float* o_c,
+                   const float* m_c, const float* l_c, const uint8_t* accept, int32_t batch,
+                   int32_t num_kv_heads, int32_t num_q_per_kv, int32_t head_dim, void* out,
+                   int32_t out_dtype, void* stream) {
+  if (batch < 0 || num_kv_heads <= 0 || num_q_per_kv <= 0 || head_dim <= 0)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if (!valid_dtype(out_dtype)) return fail(CVSA_ERR_INVALID, "out dtype unknown");
+  if (batch == 0) return CVSA_OK;
+  if (!o_d || !m_d || !l_d || !o_c || !m_c || !l_c || !accept || !out)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  return cuda_status(launch_lse_merge(o_d, m_d, l_d, o_c, m_c, l_c, accept, batch, num_kv_heads,
+                                      num_q_per_kv, head_dim, out, out_dtype,
+                                      (cudaStream_t)stream),
+                     "lse_merge launch");
+}
+
+int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
+                       const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
+                       const uint8_t* accept, const float* o_d, const float* m_d, const float* l_d,
+                       void* out, int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                       void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (max_sel <= 0) return fail(CVSA_ERR_INVALID, "max_sel must be positive");
+  if (!attend_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "decode built for block_size 16, head_dim 64/128/256, G<=16");
+  if (!valid_dtype(out_dtype)) return fail(CVSA_ERR_INVALID, "out dtype unknown");
+  if (q.B == 0) return CVSA_OK;
+  if (!page_indices || !n_per_head || !accept || !o_d || !m_d || !l_d || !out)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  const size_t need = decode_ws(q, kv, max_sel);
+  if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(CVSA_ERR_WORKSPACE, "workspace needs %zu bytes, 256-aligned", need);
+  const size_t bm_off = need - align256((size_t)q.B * kv.hkv * bitmap_words(q.W) * 4);
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(workspace) + bm_off);
+  cudaStream_t s = (cudaStream_t)stream;
+  st = cuda_status(launch_build_bitmap(page_indices, max_sel, n_per_head, q.B * kv.hkv, q.W, bitmap,
+                                       bitmap_words(q.W), nullptr, s),
+                   "bitmap launch");
+  if (st) return st;
+  AttendParams p;
+  memset(&p, 0, sizeof(p));
+  p.sel0 = page_indices;
+  p.n0 = n_per_head;
+  p.sel_stride = max_sel;
+  p.src_select = 0;
+  p.recover = true;
+  p.accept = accept;
+  p.bitmap = bitmap;
+  p.bitmap_words = bitmap_words(q.W);
+  p.external_draft = true;
+  p.ext_o = o_d;
+  p.ext_m = m_d;
+  p.ext_l = l_d;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.workspace = workspace;
+  p.ws_bytes = workspace_bytes;
+  return cuda_status(launch_attend(q, kv, p, max_sel, s, false), "recover launch");
+}
+
+size_t cvsa_step_workspace_size(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
+                                const cvsa_step_config_t* cfg, int32_t max_sel) {
+  KvView kv;
+  QView q;
+  if (check_kv(kvd, &kv) || check_q(qd, kv, false, &q) || !cfg || max_sel <= 0) return 0;
+  // size for the largest mode so one workspace serves every mode of a layer
+  StepLayout L = step_layout(q, kv, max_sel, true, false);
+  StepLayout Ld = step_layout(q, kv, max_sel, false, true);
+  return L.total > Ld.total ? L.total : Ld.total;
+}
+
+int cvsa_workspace_reset(void* workspace, size_t workspace_bytes, void* stream) {
+  if (!workspace) return fail(CVSA_ERR_INVALID, "workspace is NULL");
+  return cuda_status(cudaMemsetAsync(workspace, 0, workspace_bytes, (cudaStream_t)stream),
+                     "workspace memset");
+}
+
+int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
+                     const cvsa_step_config_t* cfg, const cvsa_step_io_t* io, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (!cfg || !io) return fail(CVSA_ERR_INVALID, "config/io is NULL");
+  const int mode = cfg->mode;
+  if (mode < CVSA_MODE_SCORE || mode > CVSA_MODE_DENSE)
+    return fail(CVSA_ERR_INVALID, "unknown mode %d", mode);
+  if (cfg->recovery != CVSA_RECOVERY_EXACT && cfg->recovery != CVSA_RECOVERY_NONE)
+    return fail(CVSA_ERR_INVALID, "unknown recovery %d", cfg->recovery);
+  if (cfg->budget < 0 || cfg->sink_pages < 0 || cfg->local_pages < 0)
+    return fail(CVSA_ERR_INVALID, "budget/sink/local must be >= 0");
+  if (!io->out) return fail(CVSA_ERR_INVALID, "out is NULL");
+  const bool dense = mode == CVSA_MODE_DENSE;
+  if (!dense) {
+    if (!io->cached_indices || !io->cached_n) return fail(CVSA_ERR_INVALID, "cached selection is NULL");
+    if (io->max_sel < cfg->budget + cfg->sink_pages + cfg->local_pages || io->max_sel <= 0)
+      return fail(CVSA_ERR_INVALID, "max_sel=%d < budget+sink+local=%d", io->max_sel,
+                  cfg->budget + cfg->sink_pages + cfg->local_pages);
+  }
+  if (!score_supported(q, kv) || !attend_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "built for block_size 16, head_dim 64/128/256, G<=16");
+  if (q.W > kMaxPagesSelect)
+    return fail(CVSA_ERR_UNSUPPORTED, "max_pages=%d above %d", q.W, kMaxPagesSelect);
+  const int max_sel = dense ? 1 : io->max_sel;
+  const size_t need = cvsa_step_workspace_size(qd, kvd, cfg, max_sel);
+  if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(CVSA_ERR_WORKSPACE, "workspace needs %zu bytes, 256-aligned", need);
+  if (q.B == 0) return CVSA_OK;
+
+  cudaStream_t s = (cudaStream_t)stream;
+  uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+  const bool recover = cfg->recovery == CVSA_RECOVERY_EXACT;
+  StepLayout L = step_layout(q, kv, max_sel, recover || true, dense);
+  void* const* ev = io->timing_events;
+  const bool pdl = ev == nullptr;
+  auto rec = [&](int i) -> int {
+    if (!ev || !ev[i]) return CVSA_OK;
+    return cuda_status(cudaEventRecord((cudaEvent_t)ev[i], s), "event record");
+  };
+
+  AttendParams ap;
+  memset(&ap, 0, sizeof(ap));
+  ap.out = io->out;
+  ap.out_dtype = q.dtype;
+  ap.counters = io->counters;
+  ap.dev_err = io->dev_error;
+  ap.workspace = ws + L.attend;
+  ap.ws_bytes = workspace_bytes - L.attend;
+
+  if (dense || mode == CVSA_MODE_REUSE) {
+    ap.dense = dense;
+    ap.sel0 = io->cached_indices;
+    ap.n0 = io->cached_n;
+    ap.sel_stride = max_sel;
+    ap.src_select = 0;
+    if (mode == CVSA_MODE_REUSE && io->step_flags) {
+      // reuse steps run no gate (backend.py:866-881)
+      st = cuda_status(cudaMemsetAsync(io->step_flags, 0, sizeof(int32_t), s), "flags");
+      if (st) return st;
+    }
+    if ((st = rec(CVSA_EV_ATTEND_BEGIN))) return st;
+    st = cuda_status(launch_attend(q, kv, ap, max_sel, s, pdl), "attend launch");
+    if (st) return st;
+    return rec(CVSA_EV_ATTEND_END);
+  }
+
+  float* scores = io->page_scores ? io->page_scores : reinterpret_cast<float*>(ws + L.scores);
+  int32_t* sel_new = reinterpret_cast<int32_t*>(ws + L.sel);
+  int32_t* n_new = reinterpret_cast<int32_t*>(ws + L.n);
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(ws + L.bitmap);
+  uint8_t* acc_new = ws + L.acc_new;
+  float* cov_new = reinterpret_cast<float*>(ws + L.cov_new);
+  uint8_t* acc_c = ws + L.acc_c;
+  float* cov_c = reinterpret_cast<float*>(ws + L.cov_c);
+  int32_t* sync = reinterpret_cast<int32_t*>(ws + L.sync);  // [0..1] sync, [2] decision
+
+  if ((st = rec(CVSA_EV_SCORE_BEGIN))) return st;
+  st = cuda_status(launch_score_pages(q, kv, scores, io->dev_error, s, pdl), "score launch");
+  if (st) return st;
+  if ((st = rec(CVSA_EV_SCORE_END))) return st;
+
+  SelectParams sp;
+  memset(&sp, 0, sizeof(sp));
+  sp.scores = scores;
+  sp.B = q.B;
+  sp.hkv = kv.hkv;
+  sp.W = q.W;
+  sp.bs = kv.bs;
+  sp.lens = q.lens;
+  sp.budget = cfg->budget;
+  sp.sink = cfg->sink_pages;
+  sp.local = cfg->local_pages;
+  sp.tau = cfg->tau;
+  sp.sel_idx = sel_new;
+  sp.sel_n = n_new;
+  sp.max_sel = max_sel;
+  sp.sel_bitmap = bitmap;
+  sp.bitmap_words = bitmap_words(q.W);
+  sp.accept = acc_new;
+  sp.cov = cov_new;
+  sp.cached_idx = io->cached_indices;
+  sp.cached_n = io->cached_n;
+  sp.cached_stride = max_sel;
+  sp.cached_accept = acc_c;
+  sp.cached_cov = cov_c;
+  sp.sync_ctr = sync;
+  sp.decision = sync + 2;
+  sp.counters = io->counters;
+  sp.mode = mode;
+  sp.has_cache = cfg->has_cache;
+  sp.lazy_stats = cfg->lazy_stats;
+  sp.step_flags = io->step_flags;
+  if ((st = rec(CVSA_EV_SELECT_BEGIN))) return st;
+  st = cuda_status(launch_select_gate(sp, s, pdl), "select launch");
+  if (st) return st;
+  if ((st = rec(CVSA_EV_SELECT_END))) return st;
+
+  ap.sel0 = io->cached_indices;
+  ap.n0 = io->cached_n;
+  ap.sel1 = sel_new;
+  ap.n1 = n_new;
+  ap.sel_stride = max_sel;
+  ap.src_select = (mode == CVSA_MODE_LAZY) ? 2 : 1;
+  ap.decision = sync + 2;
+  ap.recover = recover;
+  ap.accept = acc_new;
+  ap.bitmap = bitmap;
+  ap.bitmap_words = bitmap_words(q.W);
+  ap.commit_src1 = true;
+  ap.commit_idx = io->cached_indices;
+  ap.commit_n = io->cached_n;
+  ap.accept_out = io->accept;
+  ap.cov_out = io->coverage;
+  ap.acc0 = (mode == CVSA_MODE_LAZY) ? acc_c : nullptr;
+  ap.cov0 = (mode == CVSA_MODE_LAZY) ? cov_c : nullptr;
+  ap.acc1 = acc_new;
+  ap.cov1 = cov_new;
+  // the attend workspace must fit the recovery grid
+  if (workspace_bytes - L.attend < attend_workspace_bytes(q, kv, max_sel, recover, false))
+    return fail(CVSA_ERR_WORKSPACE, "workspace too small for recovery");
+  if ((st = rec(CVSA_EV_ATTEND_BEGIN))) return st;
+  st = cuda_status(launch_attend(q, kv, ap, max_sel, s, pdl), "attend launch");
+  if (st) return st;
+  return rec(CVSA_EV_ATTEND_END);
+}
+
+int cvsa_paged_append(const cvsa_kv_desc_t* kvd, const void* k_new, const void* v_new,
+                      int32_t batch, const int32_t* seq_ids, int32_t* block_tables,
+                      int32_t max_pages, int32_t* context_lens, int32_t* pages_allocated,
+                      const int32_t* free_list, int32_t free_list_len, int32_t* free_head,
+                      int32_t* dev_error, void* stream) {
+  KvView kv;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  if (batch < 0 || max_pages <= 0 || free_list_len < 0) return fail(CVSA_ERR_INVALID, "bad shape");
+  if (batch == 0) return CVSA_OK;
+  if (!k_new || !v_new || !block_tables || !context_lens || !pages_allocated || !free_list ||
+      !free_head)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  if ((reinterpret_cast<uintptr_t>(k_new) | reinterpret_cast<uintptr_t>(v_new)) % 16)
+    return fail(CVSA_ERR_INVALID, "k_new/v_new must be 16-byte aligned");
+  return cuda_status(launch_paged_append(kv, k_new, v_new, batch, seq_ids, block_tables, max_pages,
+                                         context_lens, pages_allocated, free_list, free_list_len,
+                                         free_head, dev_error, (cudaStream_t)stream),
+                     "append launch");
+}
+
+int cvsa_paged_gather(const cvsa_kv_desc_t* kvd, const int32_t* block_table_row, int32_t n_pages,
+                      void* k_out, void* v_out, int32_t* dev_error, void* stream) {
+  KvView kv;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  if (n_pages < 0) return fail(CVSA_ERR_INVALID, "n_pages < 0");
+  if (n_pages == 0) return CVSA_OK;
+  if (!block_table_row || !k_out) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  if ((reinterpret_cast<uintptr_t>(k_out) | reinterpret_cast<uintptr_t>(v_out)) % 16)
+    return fail(CVSA_ERR_INVALID, "outputs must be 16-byte aligned");
+  return cuda_status(launch_paged_gather(kv, block_table_row, n_pages, k_out, v_out, dev_error,
+                                         (cudaStream_t)stream),
+                     "gather launch");
+}
+
+}  // extern "C"

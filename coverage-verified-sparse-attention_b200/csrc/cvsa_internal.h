@@ -1,0 +1,141 @@
+// Internal (C++) launch interface between the C-ABI layer (abi.cu) and the
+// kernel files. Nothing here is exported from the shared library.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/cvsa_b200.h"
+
+namespace cvsa {
+
+struct KvView {
+  const void* k;
+  const void* v;
+  int dtype;
+  int num_blocks;
+  int bs;   // tokens per page
+  int hkv;  // KV heads
+  int d;    // head_dim
+  int64_t sb, st, sh;  // strides (elements): block, token, head
+};
+
+struct QView {
+  const void* q;
+  int dtype;
+  int B;
+  int hq;
+  int W;  // block-table width (max_pages)
+  const int32_t* tables;
+  const int32_t* lens;
+};
+
+int num_sms();
+int dtype_bytes(int dtype);
+
+// ---- score.cu ----
+cudaError_t launch_score_pages(const QView& q, const KvView& kv, float* scores,
+                               int32_t* dev_err, cudaStream_t s, bool pdl);
+bool score_supported(const QView& q, const KvView& kv);
+
+// ---- select.cu ----
+struct SelectParams {
+  const float* scores;        // [B, Hkv, W]
+  int B, hkv, W, bs;
+  const int32_t* lens;
+  int budget, sink, local;
+  float tau;
+  // new selection (nullable when only the cached gate is wanted)
+  int32_t* sel_idx;           // [B, Hkv, max_sel]
+  int32_t* sel_n;             // [B, Hkv]
+  int max_sel;
+  uint32_t* sel_bitmap;       // [B, Hkv, bitmap_words] or null
+  int bitmap_words;
+  uint8_t* accept;            // [B, Hkv] gate of the new selection, or null
+  float* cov;                 // [B, Hkv] or null
+  // cached selection gate (lazy mode)
+  const int32_t* cached_idx;  // [B, Hkv, cached_stride] or null
+  const int32_t* cached_n;
+  int cached_stride;
+  uint8_t* cached_accept;     // [B, Hkv] or null
+  float* cached_cov;
+  // batch-global decision & statistics
+  int32_t* sync_ctr;          // [2] zeroed: CTA-done count, reject count
+  int32_t* decision;          // [1] out: bit0 all cached heads accepted
+  int64_t* counters;          // [CVSA_NUM_COUNTERS] or null
+  int mode;                   // CVSA_MODE_SCORE / CVSA_MODE_LAZY / -1 (plain select)
+  int has_cache;
+  int lazy_stats;
+  int32_t* step_flags;        // [1] or null
+};
+cudaError_t launch_select_gate(const SelectParams& p, cudaStream_t s, bool pdl);
+
+cudaError_t launch_build_bitmap(const int32_t* idx, int max_sel, const int32_t* n, int BH, int W,
+                                uint32_t* bitmap, int words, int32_t* dev_err, cudaStream_t s);
+cudaError_t launch_check_coverage(const float* scores, int B, int hkv, int W,
+                                  const int32_t* idx, int max_sel, const int32_t* n,
+                                  float tau, uint8_t* accept, float* cov, cudaStream_t s);
+cudaError_t launch_complement(const int32_t* idx, int max_sel, const int32_t* n,
+                              const int32_t* lens, int B, int hkv, int bs,
+                              const uint8_t* accept, int32_t* comp, int max_comp,
+                              int32_t* n_comp, cudaStream_t s);
+
+// ---- attend.cu ----
+// Which page set each (b, h) attends to and what the finaliser writes.
+struct AttendParams {
+  // selection sources: src 0 = sel0/n0, src 1 = sel1/n1; `use_src1` (device
+  // word, bit0) picks src 1 when `src_select` == 2, otherwise src_select
+  // fixes the source.
+  const int32_t* sel0; const int32_t* n0;
+  const int32_t* sel1; const int32_t* n1;
+  int sel_stride;
+  int src_select;                 // 0, 1, or 2 = decided on device
+  const int32_t* decision;        // device word read when src_select == 2 (bit0: reuse src0)
+  bool dense;                     // attend all valid pages, no selection
+  // recovery (exact): heads with accept == 0 also attend their complement,
+  // read from `bitmap` of the source-1 selection.
+  bool recover;
+  const uint8_t* accept;          // [B, Hkv]
+  const uint32_t* bitmap;         // [B, Hkv, bitmap_words]
+  int bitmap_words;
+  bool external_draft;            // recover_merge: draft partial given, not recomputed
+  const float* ext_o; const float* ext_m; const float* ext_l;
+  // copy the source-1 selection into source 0 when source 1 was used
+  bool commit_src1;
+  int32_t* commit_idx; int32_t* commit_n;
+  // outputs
+  void* out; int out_dtype;       // normalised output or null
+  float* o_unnorm; float* m_out; float* l_out;  // draft partial or null
+  int64_t* counters;              // pages attended, or null
+  int32_t* dev_err;
+  // gate outputs of the selection actually decoded (nullable): source 0's
+  // gate (acc0/cov0, nullable = accepted) or source 1's (acc1/cov1)
+  uint8_t* accept_out; float* cov_out;
+  const uint8_t* acc0; const float* cov0;
+  const uint8_t* acc1; const float* cov1;
+  // workspace
+  void* workspace; size_t ws_bytes;
+};
+size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, bool recover,
+                              bool dense);
+cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& p,
+                          int max_sel, cudaStream_t s, bool pdl);
+bool attend_supported(const QView& q, const KvView& kv);
+
+// ---- merge.cu ----
+cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
+                             const float* o_c, const float* m_c, const float* l_c,
+                             const uint8_t* accept, int B, int hkv, int G, int D, void* out,
+                             int out_dtype, cudaStream_t s);
+
+// ---- paged_kv.cu ----
+cudaError_t launch_paged_append(const KvView& kv, const void* k_new, const void* v_new, int B,
+                                const int32_t* seq_ids, int32_t* tables, int W, int32_t* lens,
+                                int32_t* pages_alloc, const int32_t* free_list, int free_len,
+                                int32_t* free_head, int32_t* dev_err, cudaStream_t s);
+cudaError_t launch_paged_gather(const KvView& kv, const int32_t* row, int n_pages, void* k_out,
+                                void* v_out, int32_t* dev_err, cudaStream_t s);
+
+}  // namespace cvsa

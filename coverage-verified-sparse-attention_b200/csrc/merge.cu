@@ -1,0 +1,80 @@
+// Selective LSE merge of draft and complement partials.
+//
+// Restates cvsa/kernels/coverage.py:274-326 (and cvsa/lse_merge.py:11-54):
+// accepted heads o_d / max(l_d, 1e-6); rejected heads
+// (o_d e^{m_d-M} + o_c e^{m_c-M}) / max(l_d e^{m_d-M} + l_c e^{m_c-M}, 1e-6)
+// with M = max(m_d, m_c). The accept mask is per KV head, expanded over its G
+// query heads (q head index // G). One warp per query head, 16-byte stores.
+// A side whose m is -inf carries no mass (the reference would form NaN from
+// exp(-inf - -inf) there; its merge kernel never sees that case because
+// accepted heads skip this branch).
+#include "cvsa_common.cuh"
+#include "cvsa_internal.h"
+
+namespace cvsa {
+namespace {
+
+template <typename TO>
+__global__ void lse_merge_kernel(const float* __restrict__ o_d, const float* __restrict__ m_d,
+                                 const float* __restrict__ l_d, const float* __restrict__ o_c,
+                                 const float* __restrict__ m_c, const float* __restrict__ l_c,
+                                 const uint8_t* __restrict__ accept, int rows, int hq, int G,
+                                 int D, TO* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int b = row / hq;
+  const int qh = row % hq;
+  const int kvh = qh / G;
+  const int hkv = hq / G;
+  const bool acc = accept[b * hkv + kvh] != 0;
+  const float md = m_d[row], ld = l_d[row];
+  float sd = 1.f, sc = 0.f, denom;
+  if (acc) {
+    denom = fmaxf(ld, 1e-6f);
+  } else {
+    const float mc = m_c[row], lc = l_c[row];
+    const float M = fmaxf(md, mc);
+    sd = (md == neg_inf()) ? 0.f : expf(md - M);
+    sc = (mc == neg_inf()) ? 0.f : expf(mc - M);
+    denom = fmaxf(ld * sd + lc * sc, 1e-6f);
+  }
+  for (int d = lane; d < D; d += 32) {
+    const int64_t i = (int64_t)row * D + d;
+    float v = o_d[i] * sd;
+    if (!acc) v += o_c[i] * sc;
+    out[i] = Elem<TO>::from_f(v / denom);
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
+                             const float* o_c, const float* m_c, const float* l_c,
+                             const uint8_t* accept, int B, int hkv, int G, int D, void* out,
+                             int out_dtype, cudaStream_t s) {
+  const int rows = B * hkv * G;
+  if (rows == 0) return cudaSuccess;
+  const int wpb = 8;
+  const int grid = (rows + wpb - 1) / wpb;
+  const int hq = hkv * G;
+  switch (out_dtype) {
+    case CVSA_DTYPE_BF16:
+      lse_merge_kernel<<<grid, wpb * 32, 0, s>>>(o_d, m_d, l_d, o_c, m_c, l_c, accept, rows, hq,
+                                                 G, D, (__nv_bfloat16*)out);
+      break;
+    case CVSA_DTYPE_F16:
+      lse_merge_kernel<<<grid, wpb * 32, 0, s>>>(o_d, m_d, l_d, o_c, m_c, l_c, accept, rows, hq,
+                                                 G, D, (__half*)out);
+      break;
+    case CVSA_DTYPE_F32:
+      lse_merge_kernel<<<grid, wpb * 32, 0, s>>>(o_d, m_d, l_d, o_c, m_c, l_c, accept, rows, hq,
+                                                 G, D, (float*)out);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace cvsa

@@ -1,0 +1,339 @@
+"""CVSA attention backend on the B200 kernels (drop-in for cvsa/backend.py).
+
+`CVSABackend` keeps the reference's constructor, call signature and
+statistics (cvsa/backend.py:45-311) so the reference's decode loops use it
+unchanged. What differs is where the work happens: each layer call is ONE
+C-ABI call (cvsa_decode_step) that enqueues the whole step on the current
+stream -- page scoring, top-k selection, coverage gate, sparse decode, exact
+recovery and LSE merge -- with the lazy schedule's batch-global decision
+(backend.py:446, `accept_mask.all()`) taken on the device. There is no host
+synchronisation on the hot path, so a layer step can be captured in a CUDA
+graph; statistics live in device counters read once by get_stats().
+
+Scheduling follows the reference:
+  * dense layer          -> attention over every valid page (backend.py:327-333)
+  * lazy, step % M == 0  -> _lazy_step: fresh scores, gate the cached
+                            selection, reuse it if every (b, h) accepts, else a
+                            full scoring step (backend.py:392-465)
+  * lazy, other steps    -> _reuse_step (backend.py:866-881)
+  * fixed interval R     -> scoring step every R steps, reuse between
+                            (backend.py:361-366)
+A layer without a cached selection takes a scoring step (the reference's
+_reuse_step re-enters __call__ with step - 1 for that case).
+
+Extensions (off by default): `sink_pages` / `local_pages` always-kept pages,
+and the stable (score desc, page index asc) top-k order. Options of the
+reference that select pages differently (adaptive_selection,
+static_budget_table, selector='quest', top_p, light_normalizer), approximate
+recovery, the random-reject counterfactual and the decoupled coverage
+interval are not implemented by this backend yet and raise
+NotImplementedError when requested.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from cvsa import _lib
+from cvsa.kernels.select import budget_for
+
+
+class _LayerState:
+    __slots__ = ("key", "cached_idx", "cached_n", "has_cache", "accept", "coverage",
+                 "flags", "scores")
+
+    def __init__(self, key, B, Hkv, max_sel, W, device, keep_scores):
+        self.key = key
+        self.cached_idx = torch.zeros((B, Hkv, max_sel), dtype=torch.int32, device=device)
+        self.cached_n = torch.zeros((B, Hkv), dtype=torch.int32, device=device)
+        self.has_cache = False
+        self.accept = torch.ones((B, Hkv), dtype=torch.uint8, device=device)
+        self.coverage = torch.ones((B, Hkv), dtype=torch.float32, device=device)
+        self.flags = torch.zeros((1,), dtype=torch.int32, device=device)
+        self.scores = (torch.empty((B, Hkv, W), dtype=torch.float32, device=device)
+                       if keep_scores else None)
+
+
+class CVSABackend:
+    """CVSA backend: draft with sparse attention, verify with coverage, recover."""
+
+    def __init__(
+        self,
+        num_kv_heads: int,
+        num_q_heads: int,
+        head_dim: int,
+        block_size: int,
+        num_layers: int = 32,
+        budget_pct: float = 0.10,
+        reuse_interval: int = 16,
+        coverage_threshold: float = 0.90,
+        dense_layers: Optional[List[int]] = None,
+        lazy: bool = False,
+        check_interval: Optional[int] = None,
+        coverage_interval: Optional[int] = None,
+        approx_recovery_pct: Optional[float] = None,
+        adaptive_selection: bool = False,
+        adaptive_floor_ratio: float = 0.5,
+        random_reject_prob: Optional[float] = None,
+        static_budget_table: Optional[Dict[int, List[float]]] = None,
+        selector: str = "exact",
+        top_p: Optional[float] = None,
+        light_normalizer: bool = False,
+        sink_pages: int = 0,
+        local_pages: int = 0,
+        keep_page_scores: bool = False,
+    ):
+        # argument checks of the reference (backend.py:150-178)
+        if selector not in ("exact", "quest"):
+            raise ValueError(f"Unknown selector: {selector!r}")
+        if light_normalizer and selector != "quest":
+            raise ValueError(
+                "light_normalizer=True requires selector='quest' "
+                "(the sketch supplies both selection and normalizer)")
+        if top_p is not None and not (0.0 < top_p < 1.0):
+            raise ValueError(f"top_p must be in (0, 1), got {top_p}")
+        if num_q_heads % num_kv_heads:
+            raise ValueError("num_q_heads must be a multiple of num_kv_heads")
+        if sink_pages < 0 or local_pages < 0:
+            raise ValueError("sink_pages/local_pages must be >= 0")
+        unsupported = []
+        if approx_recovery_pct is not None:
+            unsupported.append("approx_recovery_pct")
+        if adaptive_selection:
+            unsupported.append("adaptive_selection")
+        if random_reject_prob is not None:
+            unsupported.append("random_reject_prob")
+        if static_budget_table is not None:
+            unsupported.append("static_budget_table")
+        if selector != "exact":
+            unsupported.append("selector='quest'")
+        if top_p is not None:
+            unsupported.append("top_p")
+        if lazy and coverage_interval is not None and coverage_interval != (check_interval or 1):
+            unsupported.append("coverage_interval != check_interval")
+        if unsupported:
+            raise NotImplementedError("not implemented by the B200 backend: " +
+                                      ", ".join(unsupported))
+
+        self.num_kv_heads = num_kv_heads
+        self.num_q_heads = num_q_heads
+        self.head_dim = head_dim
+        self.block_size = block_size
+        self.num_layers = num_layers
+        self.num_q_per_kv = num_q_heads // num_kv_heads
+        self.budget_pct = budget_pct
+        self.reuse_interval = reuse_interval
+        self.tau = coverage_threshold
+        self._dense_layers = set(dense_layers or [])
+        self.approx_recovery_pct = approx_recovery_pct
+        self.lazy = lazy
+        self.check_interval = check_interval or 1
+        self.coverage_interval = coverage_interval or self.check_interval
+        self.adaptive_selection = adaptive_selection
+        self.adaptive_floor_ratio = adaptive_floor_ratio
+        self.random_reject_prob = random_reject_prob
+        self.static_budget_table = static_budget_table
+        self.selector = selector
+        self.top_p = top_p
+        self.light_normalizer = light_normalizer
+        self.sink_pages = sink_pages
+        self.local_pages = local_pages
+        self.keep_page_scores = keep_page_scores
+
+        self._layers: Dict[int, _LayerState] = {}
+        self._counters: Optional[torch.Tensor] = None   # int64[8] device
+        self._dev_error: Optional[torch.Tensor] = None
+        self._step = 0
+        self._dense_layer_steps = 0
+        self._last_accept_mask: Dict[int, Optional[torch.Tensor]] = {}
+        self._last_expanded_selection: Dict[int, Optional[Tuple[torch.Tensor, torch.Tensor]]] = {}
+        self._track_timing = False
+        self._timing_events = None   # caller-owned cudaEvent_t array (bench.py)
+        self._pending_events: list = []
+        self._kernel_times_ms = {"scoring": 0.0, "coverage": 0.0, "sparse_draft": 0.0,
+                                 "ar_recovery": 0.0, "dense": 0.0}
+        self._kernel_counts = {k: 0 for k in self._kernel_times_ms}
+
+    # ---- bookkeeping (backend.py:225-311) -------------------------------
+    def enable_timing(self, track: bool = True):
+        """Per-kernel CUDA-event timing (backend.py:225-250). Buckets: 'scoring'
+        (page scoring), 'coverage' (top-k selection + coverage gate),
+        'sparse_draft' (attention of reuse steps), 'ar_recovery' (attention of
+        scoring steps: draft + complement recovery + merge, one kernel) and
+        'dense'. Recording events between kernels disables launch overlap."""
+        self._track_timing = track
+
+    def _flush_timing(self):
+        if not self._pending_events:
+            return
+        torch.cuda.synchronize()
+        for mode, ev in self._pending_events:
+            pairs = []
+            if mode in (_lib.MODE_SCORE, _lib.MODE_LAZY):
+                pairs = [("scoring", _lib.EV_SCORE_BEGIN), ("coverage", _lib.EV_SELECT_BEGIN),
+                         ("ar_recovery", _lib.EV_ATTEND_BEGIN)]
+            elif mode == _lib.MODE_REUSE:
+                pairs = [("sparse_draft", _lib.EV_ATTEND_BEGIN)]
+            else:
+                pairs = [("dense", _lib.EV_ATTEND_BEGIN)]
+            for name, i in pairs:
+                self._kernel_times_ms[name] += ev[i].elapsed_time(ev[i + 1])
+                self._kernel_counts[name] += 1
+        self._pending_events.clear()
+
+    def reset(self):
+        self._step = 0
+        for st in self._layers.values():
+            st.has_cache = False
+        self._last_accept_mask = {}
+        self._last_expanded_selection = {}
+        if self._counters is not None:
+            self._counters.zero_()
+        if self._dev_error is not None:
+            self._dev_error.zero_()
+        self._dense_layer_steps = 0
+        for k in self._kernel_times_ms:
+            self._kernel_times_ms[k] = 0.0
+            self._kernel_counts[k] = 0
+        self._pending_events.clear()
+
+    @property
+    def is_scoring_step(self):
+        return self._step % self.reuse_interval == 0
+
+    def step_done(self, layer_idx: int, num_layers: int):
+        if layer_idx == num_layers - 1:
+            self._step += 1
+
+    def _counter_values(self) -> List[int]:
+        if self._counters is None:
+            return [0] * _lib.NUM_COUNTERS
+        return [int(x) for x in self._counters.tolist()]
+
+    def get_stats(self) -> dict:
+        c = self._counter_values()
+        scoring = c[_lib.CTR_SCORING_STEPS]
+        checks = c[_lib.CTR_COVERAGE_CHECKS]
+        total_checks = max(checks, scoring, 1)
+        stats = {
+            "total_scoring_steps": scoring,
+            "total_coverage_checks": checks,
+            "all_accepted_pct": c[_lib.CTR_ACCEPT_STEPS] / total_checks * 100,
+            "some_rejected_pct": c[_lib.CTR_REJECT_STEPS] / total_checks * 100,
+            "per_head_accept_rate": c[_lib.CTR_HEAD_ACCEPT] / max(c[_lib.CTR_HEAD_TOTAL], 1) * 100,
+            "total_decode_steps": self._step,
+            "lazy": self.lazy,
+            "check_interval": self.check_interval if self.lazy else None,
+            "rescore_rate": scoring / max(checks, 1) * 100 if self.lazy else 100.0,
+            "dense_layer_steps": self._dense_layer_steps,
+        }
+        if c[_lib.CTR_PAGES_MAX] > 0:
+            stats["effective_budget_pct"] = c[_lib.CTR_PAGES_ATTENDED] / c[_lib.CTR_PAGES_MAX] * 100
+            stats["total_pages_attended"] = c[_lib.CTR_PAGES_ATTENDED]
+            stats["total_pages_max"] = c[_lib.CTR_PAGES_MAX]
+        if self._track_timing:
+            self._flush_timing()
+            n_decode = max(self._step, 1)
+            stats["kernel_times_ms_total"] = dict(self._kernel_times_ms)
+            stats["kernel_counts"] = dict(self._kernel_counts)
+            stats["kernel_ms_per_decode_step"] = {
+                k: v / n_decode for k, v in self._kernel_times_ms.items()}
+        return stats
+
+    def device_errors(self) -> int:
+        """CVSA_DEV_ERR_* bits raised by the kernels so far (synchronises)."""
+        return 0 if self._dev_error is None else int(self._dev_error.item())
+
+    # ---- the step --------------------------------------------------------
+    def _ensure(self, device: torch.device):
+        if self._counters is None or self._counters.device != device:
+            self._counters = torch.zeros((_lib.NUM_COUNTERS,), dtype=torch.int64, device=device)
+            self._dev_error = torch.zeros((1,), dtype=torch.int32, device=device)
+
+    def _layer_state(self, layer_idx, B, W, max_sel, device) -> _LayerState:
+        key = (B, W, max_sel, device)
+        st = self._layers.get(layer_idx)
+        if st is None or st.key != key:
+            st = _LayerState(key, B, self.num_kv_heads, max_sel, W, device, self.keep_page_scores)
+            self._layers[layer_idx] = st
+        return st
+
+    def _mode_for(self, layer_idx: int, st: _LayerState) -> int:
+        if layer_idx in self._dense_layers:
+            return _lib.MODE_DENSE
+        if self.lazy:
+            if self._step % self.check_interval == 0 or not st.has_cache:
+                return _lib.MODE_LAZY
+            return _lib.MODE_REUSE
+        if self._step % self.reuse_interval == 0 or not st.has_cache:
+            return _lib.MODE_SCORE
+        return _lib.MODE_REUSE
+
+    def __call__(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                 block_tables: torch.Tensor, context_lens: torch.Tensor,
+                 layer_idx: int) -> torch.Tensor:
+        self._last_accept_mask.pop(layer_idx, None)
+        self._last_expanded_selection.pop(layer_idx, None)
+        if q.dim() == 4:
+            q = q.squeeze(1)
+        dev = _lib.require_cuda(q, k_cache, v_cache, block_tables, context_lens)
+        self._ensure(dev)
+        B, Hq, D = q.shape
+        W = block_tables.shape[1]
+        budget = budget_for(W, self.budget_pct)
+        max_sel = budget + self.sink_pages + self.local_pages
+        st = self._layer_state(layer_idx, B, W, max_sel, dev)
+        mode = self._mode_for(layer_idx, st)
+        if mode == _lib.MODE_DENSE:
+            self._dense_layer_steps += 1
+
+        q = q.contiguous()
+        bt = block_tables if block_tables.dtype == torch.int32 else block_tables.to(torch.int32)
+        cl = context_lens if context_lens.dtype == torch.int32 else context_lens.to(torch.int32)
+        bt = bt.contiguous()
+        cl = cl.contiguous()
+        out = torch.empty_like(q)
+        kvd = _lib.kv_desc(k_cache, v_cache)
+        qd = _lib.query_desc(q, bt, cl)
+        cfg = _lib.StepConfig(mode, budget, self.sink_pages, self.local_pages, float(self.tau),
+                              _lib.RECOVERY_EXACT, 1 if st.has_cache else 0,
+                              1 if self.lazy else 0)
+        io = _lib.StepIO(st.cached_idx.data_ptr(), st.cached_n.data_ptr(), max_sel, 0,
+                         out.data_ptr(), _lib.ptr(st.scores), st.accept.data_ptr(),
+                         st.coverage.data_ptr(), self._counters.data_ptr(), st.flags.data_ptr(),
+                         self._dev_error.data_ptr())
+        lib = _lib.load()
+        nbytes = lib.cvsa_step_workspace_size(qd, kvd, cfg, max_sel)
+        ws = _lib.WORKSPACE.get(nbytes, dev, "step")
+        stream = _lib.stream_ptr(dev)
+        events = None
+        if self._timing_events is not None:
+            io.timing_events = ctypes.cast(self._timing_events, ctypes.c_void_p)
+        elif self._track_timing:
+            events = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NUM_EVENTS)]
+            arr = (ctypes.c_void_p * _lib.NUM_EVENTS)(*[e.cuda_event for e in events])
+            io.timing_events = ctypes.cast(arr, ctypes.c_void_p)
+        _lib.check(lib.cvsa_decode_step(qd, kvd, cfg, io, ws.data_ptr(), ws.numel(), stream),
+                   "cvsa_decode_step")
+        if events is not None:
+            self._pending_events.append((mode, events))
+        if mode in (_lib.MODE_SCORE, _lib.MODE_LAZY):
+            st.has_cache = True
+            self._last_accept_mask[layer_idx] = st.accept.bool()
+        return out
+
+    # ---- tracing helpers -------------------------------------------------
+    def cached_selection(self, layer_idx: int) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+        """(page_indices [B,H_kv,max_sel] ascending, n_per_head) cached for a layer."""
+        st = self._layers.get(layer_idx)
+        if st is None or not st.has_cache:
+            return None
+        return st.cached_idx, st.cached_n
+
+    def last_step_flags(self, layer_idx: int) -> Optional[torch.Tensor]:
+        """Device word: bit0 every head accepted, bit1 the selection was rescored."""
+        st = self._layers.get(layer_idx)
+        return None if st is None else st.flags

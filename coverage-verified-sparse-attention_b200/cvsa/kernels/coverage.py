@@ -1,0 +1,84 @@
+"""Complement indices, coverage gate and LSE merge.
+
+Drop-in for cvsa/kernels/coverage.py: `triton_compute_complement` (:99-150),
+`triton_check_coverage` (:218-265) and `triton_lse_merge` (:329-367), backed
+by csrc/select.cu and csrc/merge.cu.
+"""
+
+from typing import Tuple
+
+import torch
+
+from cvsa import _lib
+
+
+def _n_valid_max(context_lens: torch.Tensor, block_size: int) -> int:
+    # the reference also syncs here (coverage.py:121)
+    return int(((int(context_lens.max().item()) + block_size - 1) // block_size))
+
+
+def compute_complement(page_indices: torch.Tensor, n_per_head: torch.Tensor,
+                       context_lens: torch.Tensor, block_size: int,
+                       accept_mask: torch.Tensor = None,
+                       max_comp: int = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Valid pages not selected, ascending; n = 0 for accepted heads.
+
+    Returns (complement [B, H_kv, max_comp] int32, n_complement [B, H_kv] int32).
+    max_comp defaults to the largest n_valid (one host sync, as the reference).
+    """
+    dev = _lib.require_cuda(page_indices, n_per_head, context_lens, accept_mask)
+    B, H, K = page_indices.shape
+    if max_comp is None:
+        max_comp = max(_n_valid_max(context_lens, block_size), 1)
+    pi = page_indices.to(torch.int32).contiguous()
+    nph = n_per_head.to(torch.int32).contiguous()
+    am = None if accept_mask is None else accept_mask.to(torch.uint8).contiguous()
+    comp = torch.zeros((B, H, max_comp), dtype=torch.int32, device=dev)
+    n_comp = torch.zeros((B, H), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.cvsa_compute_complement(pi.data_ptr(), K, nph.data_ptr(),
+                                           context_lens.data_ptr(), B, H, block_size,
+                                           _lib.ptr(am), comp.data_ptr(), max_comp,
+                                           n_comp.data_ptr(), _lib.stream_ptr(dev)),
+               "cvsa_compute_complement")
+    return comp, n_comp
+
+
+def check_coverage(page_scores: torch.Tensor, selected_indices: torch.Tensor,
+                   n_per_head: torch.Tensor, tau: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    """(accept_mask [B, H_kv] bool, coverage [B, H_kv] float32)."""
+    dev = _lib.require_cuda(page_scores, selected_indices, n_per_head)
+    B, H, W = page_scores.shape
+    K = selected_indices.shape[2]
+    ps = page_scores.float().contiguous()
+    si = selected_indices.to(torch.int32).contiguous()
+    nph = n_per_head.to(torch.int32).contiguous()
+    acc = torch.empty((B, H), dtype=torch.uint8, device=dev)
+    cov = torch.empty((B, H), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.cvsa_check_coverage(ps.data_ptr(), B, H, W, si.data_ptr(), K, nph.data_ptr(),
+                                       float(tau), acc.data_ptr(), cov.data_ptr(),
+                                       _lib.stream_ptr(dev)), "cvsa_check_coverage")
+    return acc.bool(), cov
+
+
+def lse_merge(o_draft, m_draft, l_draft, o_comp, m_comp, l_comp, accept_mask,
+              num_kv_heads: int, num_q_per_kv: int,
+              output_dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Selective LSE merge -> [B, H_q, D] in output_dtype."""
+    dev = _lib.require_cuda(o_draft, m_draft, l_draft, o_comp, m_comp, l_comp, accept_mask)
+    B, Hq, D = o_draft.shape
+    args = [t.float().contiguous() for t in (o_draft, m_draft, l_draft, o_comp, m_comp, l_comp)]
+    am = accept_mask.to(torch.uint8).contiguous()
+    out = torch.empty((B, Hq, D), dtype=output_dtype, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.cvsa_lse_merge(*[a.data_ptr() for a in args], am.data_ptr(), B, num_kv_heads,
+                                  num_q_per_kv, D, out.data_ptr(), _lib.dtype_code(output_dtype),
+                                  _lib.stream_ptr(dev)), "cvsa_lse_merge")
+    return out
+
+
+# Reference names.
+triton_compute_complement = compute_complement
+triton_check_coverage = check_coverage
+triton_lse_merge = lse_merge

@@ -1,0 +1,297 @@
+/*
+ * cvsa_b200.h -- C ABI of the B200-native CVSA decode step (libcvsa_b200.so).
+ *
+ * The CVSA decode step of DJ-Melvin/coverage-verified-sparse-attention is:
+ * page scoring -> top-k page selection -> sparse paged decode emitting
+ * (o, LSE) -> per-head coverage gate against tau -> complement recovery merged
+ * by LSE. Every entry point below replaces one function of the reference's
+ * Python/Triton call surface; the reference file:line is given beside each.
+ *
+ * Conventions (all entry points):
+ *   - All tensor pointers are DEVICE pointers on the current CUDA device.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ *     stream). Every call only enqueues work on that stream; nothing blocks
+ *     the host and nothing allocates memory: scratch comes from a
+ *     caller-provided workspace whose size is queried with *_workspace_size.
+ *   - Integer tensors are int32 unless stated; layouts are row-major and
+ *     contiguous unless a stride is passed.
+ *   - Return value: CVSA_OK (0) or a negative CVSA_ERR_* status; the message
+ *     of the last failing call on this host thread is cvsa_last_error().
+ *     Bad arguments return CVSA_ERR_INVALID (the reference raises ValueError);
+ *     an exhausted page pool is CVSA_ERR_POOL (the reference asserts).
+ *   - Device-side bounds checks (block ids, page indices) never trap: they
+ *     record CVSA_DEV_ERR_* bits in a caller-visible error word and skip the
+ *     access.
+ */
+#ifndef CVSA_B200_H_
+#define CVSA_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CVSA_ABI_VERSION 1
+
+/* element types */
+enum {
+  CVSA_DTYPE_F32 = 0,
+  CVSA_DTYPE_F16 = 1,
+  CVSA_DTYPE_BF16 = 2
+};
+
+/* status codes */
+enum {
+  CVSA_OK = 0,
+  CVSA_ERR_INVALID = -1,     /* bad argument (reference: ValueError) */
+  CVSA_ERR_UNSUPPORTED = -2, /* valid but not built (head_dim, block_size, GQA) */
+  CVSA_ERR_WORKSPACE = -3,   /* workspace NULL, too small or misaligned */
+  CVSA_ERR_CUDA = -4,        /* a CUDA runtime call or launch failed */
+  CVSA_ERR_POOL = -5         /* page pool exhausted (reference: assert) */
+};
+
+/* bits of the device error word (cvsa_decode_step io.dev_error, append) */
+enum {
+  CVSA_DEV_ERR_BLOCK_RANGE = 1, /* a block table entry outside [0, num_blocks) */
+  CVSA_DEV_ERR_PAGE_RANGE = 2,  /* a page index outside [0, max_pages) */
+  CVSA_DEV_ERR_POOL = 4,        /* append: free list exhausted */
+  CVSA_DEV_ERR_TABLE_FULL = 8,  /* append: sequence longer than the table */
+  CVSA_DEV_ERR_TIMEOUT = 16     /* a bounded wait on an async copy gave up */
+};
+
+/* Paged KV pool: [num_blocks, block_size, num_kv_heads, head_dim].
+ * cvsa/runtime/kv_cache.py:24-50 (PagedKVCache.k_cache / v_cache). v_cache
+ * shares k_cache's strides. head_dim is contiguous; rows must be 16-byte
+ * aligned. */
+typedef struct cvsa_kv_desc {
+  const void* k_cache;
+  const void* v_cache;
+  int32_t dtype;
+  int32_t num_blocks;
+  int32_t block_size;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  int32_t reserved0;
+  int64_t stride_block; /* elements */
+  int64_t stride_token; /* elements */
+  int64_t stride_head;  /* elements */
+} cvsa_kv_desc_t;
+
+/* Decode queries and per-sequence page tables.
+ * q: [batch, num_q_heads, head_dim] contiguous (cvsa/backend.py:315).
+ * block_tables: [batch, max_pages] (kv_cache.py:96-100); context_lens: [batch]. */
+typedef struct cvsa_query_desc {
+  const void* q;
+  int32_t dtype;
+  int32_t batch;
+  int32_t num_q_heads;
+  int32_t max_pages;
+  const int32_t* block_tables;
+  const int32_t* context_lens;
+} cvsa_query_desc_t;
+
+int cvsa_abi_version(void);
+const char* cvsa_status_string(int status);
+const char* cvsa_last_error(void);
+
+/* Page scores, [batch, num_kv_heads, max_pages] float32:
+ * max over valid tokens of (mean-pooled GQA q, rounded to q's dtype) . k,
+ * times head_dim^-0.5; -inf at and beyond the context.
+ * Replaces triton_score_pages, cvsa/kernels/page_scores.py:77-119
+ * (kernel :13-74). */
+int cvsa_score_pages(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                     float* page_scores, void* stream);
+
+/* Top-k page selection per (b, kv head): the first `sink_pages` and last
+ * `local_pages` valid pages, plus the `budget` highest-scoring other valid
+ * pages, ordered (score desc, page index asc); written in ascending page
+ * order into page_indices [batch, num_kv_heads, max_sel] with the count in
+ * n_per_head [batch, num_kv_heads]. max_sel >= budget + sink + local.
+ * Replaces cvsa/backend.py:690,737-747 (torch.topk + n_per_head clamp). */
+int cvsa_select_pages(const float* page_scores, int32_t batch, int32_t num_kv_heads,
+                      int32_t max_pages, const int32_t* context_lens, int32_t block_size,
+                      int32_t budget, int32_t sink_pages, int32_t local_pages,
+                      int32_t* page_indices, int32_t max_sel, int32_t* n_per_head,
+                      void* stream);
+
+/* Coverage gate: cov = exp(lse(scores[sel[:n]]) - lse(scores[:max_pages])),
+ * accept = cov >= tau (uint8 0/1), both [batch, num_kv_heads].
+ * Replaces triton_check_coverage, cvsa/kernels/coverage.py:218-265
+ * (kernel :160-215). */
+int cvsa_check_coverage(const float* page_scores, int32_t batch, int32_t num_kv_heads,
+                        int32_t max_pages, const int32_t* page_indices, int32_t max_sel,
+                        const int32_t* n_per_head, float tau, uint8_t* accept,
+                        float* coverage, void* stream);
+
+/* Complement: valid pages not in the first n_per_head selected pages, in
+ * ascending order, into complement [batch, num_kv_heads, max_comp];
+ * n_complement = 0 for heads with accept != 0 (accept may be NULL).
+ * Replaces triton_compute_complement, cvsa/kernels/coverage.py:99-150, and
+ * compute_complement_pages, cvsa/complement.py:11-69. */
+int cvsa_compute_complement(const int32_t* page_indices, int32_t max_sel,
+                            const int32_t* n_per_head, const int32_t* context_lens,
+                            int32_t batch, int32_t num_kv_heads, int32_t block_size,
+                            const uint8_t* accept, int32_t* complement, int32_t max_comp,
+                            int32_t* n_complement, void* stream);
+
+/* Workspace bytes for cvsa_sparse_decode / cvsa_recover_merge with these
+ * shapes (max_sel = width of page_indices). */
+size_t cvsa_decode_workspace_size(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                                  int32_t max_sel);
+
+/* Sparse paged decode over the first n_per_head[b,h] pages of page_indices
+ * [batch, num_kv_heads, max_sel], all G query heads of a KV head at once.
+ * Writes, for each non-NULL output:
+ *   o_unnorm [batch, num_q_heads, head_dim] f32, m [batch, num_q_heads] f32
+ *   (max scaled logit), l [batch, num_q_heads] f32 (sum exp(s - m));
+ *   out [batch, num_q_heads, head_dim] in out_dtype = o / max(l, 1e-6).
+ * A head with no valid token yields (0, -inf, 0) and out = 0.
+ * Replaces triton_sparse_decode_unnorm (sparse_decode.py:537-573, kernels
+ * :424-500, :609-661, :136-234, :577-606), triton_sparse_decode_reuse
+ * (:681-721) and triton_sparse_decode (:286-350). */
+int cvsa_sparse_decode(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                       const int32_t* page_indices, int32_t max_sel,
+                       const int32_t* n_per_head, float* o_unnorm, float* m, float* l,
+                       void* out, int32_t out_dtype, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Selective LSE merge of draft (o_d, m_d, l_d) and complement (o_c, m_c, l_c)
+ * partials, [batch, G*num_kv_heads(, head_dim)] f32, with accept
+ * [batch, num_kv_heads] (uint8): accepted heads o_d / max(l_d, 1e-6), others
+ * the LSE merge divided by max(l, 1e-6). out in out_dtype.
+ * Replaces triton_lse_merge, cvsa/kernels/coverage.py:329-367 (kernel
+ * :274-326), and selective_lse_merge, cvsa/lse_merge.py:11-54. */
+int cvsa_lse_merge(const float* o_d, const float* m_d, const float* l_d,
+                   const float* o_c, const float* m_c, const float* l_c,
+                   const uint8_t* accept, int32_t batch, int32_t num_kv_heads,
+                   int32_t num_q_per_kv, int32_t head_dim, void* out, int32_t out_dtype,
+                   void* stream);
+
+/* Fused exact recovery: for heads with accept == 0, attend to the valid pages
+ * NOT in the selection (skipped through a selection bitmap, never
+ * materialised as an index list) and LSE-merge that complement partial with
+ * the given draft partial; accepted heads get o_d / max(l_d, 1e-6).
+ * Replaces cvsa/backend.py:819-842 (triton_compute_complement +
+ * triton_sparse_decode_unnorm on the complement + triton_lse_merge). */
+int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                       const int32_t* page_indices, int32_t max_sel,
+                       const int32_t* n_per_head, const uint8_t* accept,
+                       const float* o_d, const float* m_d, const float* l_d, void* out,
+                       int32_t out_dtype, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* ---- fused whole-layer step (cvsa/backend.py:313-366) ---------------- */
+
+enum {
+  CVSA_MODE_SCORE = 0, /* _scoring_step (backend.py:683-864): fresh selection */
+  CVSA_MODE_LAZY = 1,  /* _lazy_step (backend.py:392-465): gate the cached
+                          selection on fresh scores; reuse it if every
+                          (b, h) accepts, else a full scoring step */
+  CVSA_MODE_REUSE = 2, /* _reuse_step (backend.py:866-881): cached selection */
+  CVSA_MODE_DENSE = 3  /* dense layer (cvsa/runtime/dense.py:70-111) */
+};
+
+enum {
+  CVSA_RECOVERY_EXACT = 0, /* complement + LSE merge (backend.py:818-844) */
+  CVSA_RECOVERY_NONE = 1   /* rejected heads keep the draft */
+};
+
+/* device counters accumulated by cvsa_decode_step (int64 each) */
+enum {
+  CVSA_CTR_PAGES_ATTENDED = 0, /* backend.py:368-390 _attn_work */
+  CVSA_CTR_PAGES_MAX = 1,      /* _attn_work_max: sum n_valid * num_kv_heads */
+  CVSA_CTR_HEAD_ACCEPT = 2,    /* _per_head_accept_sum */
+  CVSA_CTR_HEAD_TOTAL = 3,     /* _per_head_total */
+  CVSA_CTR_ACCEPT_STEPS = 4,   /* _accept_counts */
+  CVSA_CTR_REJECT_STEPS = 5,   /* _reject_counts */
+  CVSA_CTR_SCORING_STEPS = 6,  /* _total_scoring_steps */
+  CVSA_CTR_COVERAGE_CHECKS = 7,/* _total_coverage_checks */
+  CVSA_NUM_COUNTERS = 8
+};
+
+typedef struct cvsa_step_config {
+  int32_t mode;          /* CVSA_MODE_* */
+  int32_t budget;        /* top-k budget: max(3, int(max_pages * budget_pct)) */
+  int32_t sink_pages;    /* forced leading pages (0 = reference behaviour) */
+  int32_t local_pages;   /* forced trailing pages (0 = reference behaviour) */
+  float tau;             /* coverage threshold */
+  int32_t recovery;      /* CVSA_RECOVERY_* */
+  int32_t has_cache;     /* LAZY: cached_* holds this layer's selection */
+  int32_t lazy_stats;    /* 1: count stats the way lazy mode does
+                            (backend.py:420-465), 0: the fixed-interval way
+                            (backend.py:775-862) */
+} cvsa_step_config_t;
+
+typedef struct cvsa_step_io {
+  int32_t* cached_indices; /* [batch, num_kv_heads, max_sel] in/out (_cached_selection) */
+  int32_t* cached_n;       /* [batch, num_kv_heads] in/out */
+  int32_t max_sel;         /* >= budget + sink_pages + local_pages */
+  int32_t reserved0;
+  void* out;               /* [batch, num_q_heads, head_dim], q dtype */
+  float* page_scores;      /* [batch, num_kv_heads, max_pages] out, or NULL */
+  uint8_t* accept;         /* [batch, num_kv_heads] gate of the selection decoded, or NULL */
+  float* coverage;         /* [batch, num_kv_heads] or NULL */
+  int64_t* counters;       /* [CVSA_NUM_COUNTERS] accumulated, or NULL */
+  int32_t* step_flags;     /* [1]: bit0 every head accepted, bit1 rescored; or NULL */
+  int32_t* dev_error;      /* [1]: CVSA_DEV_ERR_* bits OR-ed in, or NULL */
+  /* Optional per-kernel timing (backend.py:225-250): NULL, or CVSA_NUM_EVENTS
+   * cudaEvent_t handles recorded on `stream` around the scoring, selection/
+   * gate and attention kernels (begin, end each). Kernels a mode does not run
+   * leave their pair unrecorded. Timing disables launch overlap (PDL). */
+  void* const* timing_events;
+} cvsa_step_io_t;
+
+enum {
+  CVSA_EV_SCORE_BEGIN = 0, CVSA_EV_SCORE_END = 1,
+  CVSA_EV_SELECT_BEGIN = 2, CVSA_EV_SELECT_END = 3,
+  CVSA_EV_ATTEND_BEGIN = 4, CVSA_EV_ATTEND_END = 5,
+  CVSA_NUM_EVENTS = 6
+};
+
+size_t cvsa_step_workspace_size(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                                const cvsa_step_config_t* cfg, int32_t max_sel);
+
+/* One CVSA attention step for one layer, entirely on the device: no host
+ * synchronisation, so the call can be captured in a CUDA graph. The batch-
+ * global lazy decision (backend.py:446, accept_mask.all()) is taken on the
+ * device. The workspace must be zeroed once before its first use
+ * (cvsa_workspace_reset); the kernels leave their counters zeroed. */
+int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                     const cvsa_step_config_t* cfg, const cvsa_step_io_t* io,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Zero a workspace (cudaMemsetAsync). */
+int cvsa_workspace_reset(void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- paged KV runtime (cvsa/runtime/kv_cache.py) -------------------- */
+
+/* Append one token's K/V [batch, num_kv_heads, head_dim] (kv dtype) for each
+ * of `batch` sequences. For sequence b: position = context_lens[b]; when the
+ * position starts a new page past pages_allocated[b], a block is popped from
+ * free_list[*free_head] (atomically) and written to block_tables[b, page].
+ * Then K/V are written and context_lens[b] is incremented. seq_ids (nullable)
+ * maps row b of k_new/v_new to a sequence slot.
+ * Replaces SequenceKVManager.append_token_kv, kv_cache.py:133-150, and
+ * PagedKVCache.allocate_blocks/write_kv, kv_cache.py:53-71, as one launch.
+ * Pool exhaustion sets CVSA_DEV_ERR_POOL in *dev_error. */
+int cvsa_paged_append(const cvsa_kv_desc_t* kv, const void* k_new, const void* v_new,
+                      int32_t batch, const int32_t* seq_ids, int32_t* block_tables,
+                      int32_t max_pages, int32_t* context_lens, int32_t* pages_allocated,
+                      const int32_t* free_list, int32_t free_list_len, int32_t* free_head,
+                      int32_t* dev_error, void* stream);
+
+/* Gather the K (and V) pages of `n_pages` logical pages of one sequence into
+ * a dense [n_pages * block_size, num_kv_heads, head_dim] buffer (nullable
+ * v_out). A block id outside the pool sets CVSA_DEV_ERR_BLOCK_RANGE.
+ * The gather counterpart of PagedKVCache.write_kv_block, kv_cache.py:73-80. */
+int cvsa_paged_gather(const cvsa_kv_desc_t* kv, const int32_t* block_table_row,
+                      int32_t n_pages, void* k_out, void* v_out, int32_t* dev_error,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CVSA_B200_H_ */
