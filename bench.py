@@ -312,6 +312,8 @@ def run_cvsa(args, ws, rank, local):
     def step_events(be2):
         for l, wl in enumerate(wls):
             evs = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NUM_EVENTS)]
+            for e in evs:
+                e.record()      # torch creates the cudaEvent_t at its first record
             arr = (__import__("ctypes").c_void_p * _lib.NUM_EVENTS)(
                 *[e.cuda_event for e in evs])
             be2._timing_events = arr
@@ -336,7 +338,7 @@ def run_cvsa(args, ws, rank, local):
                 kern["select"].append(e[_lib.EV_SELECT_BEGIN].elapsed_time(e[_lib.EV_SELECT_END]))
                 kern["attend_scoring"].append(
                     e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END]))
-            except RuntimeError:
+            except (RuntimeError, ValueError):   # score/select pairs unrecorded: reuse step
                 kern["attend_reuse"].append(
                     e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END]))
     score_ms = statistics.mean(kern["score"]) if kern["score"] else None

@@ -100,6 +100,8 @@ int check_q(const cvsa_query_desc_t* qd, const KvView& kv, bool need_q, QView* o
     return fail(CVSA_ERR_INVALID, "block_tables/context_lens is NULL");
   if (need_q && (reinterpret_cast<uintptr_t>(qd->q) % 16))
     return fail(CVSA_ERR_INVALID, "q must be 16-byte aligned");
+  if ((int64_t)qd->batch * kv.hkv > kMaxHeadsPerCall)
+    return fail(CVSA_ERR_UNSUPPORTED, "batch * num_kv_heads above %d", kMaxHeadsPerCall);
   out->q = qd->q;
   out->dtype = qd->dtype;
   out->B = qd->batch;
@@ -117,21 +119,35 @@ constexpr int kMaxPagesSelect = 40000;
 
 int bitmap_words(int W) { return (W + 31) / 32; }
 
-size_t decode_ws(const QView& q, const KvView& kv, int max_sel) {
+// Decode / recovery workspace: [sync region][item partials][selection bitmap].
+struct DecodeLayout {
+  size_t partials, partial_bytes, bitmap, total;
+};
+
+DecodeLayout decode_layout(const QView& q, const KvView& kv, int max_sel) {
+  DecodeLayout L;
   size_t a = attend_workspace_bytes(q, kv, max_sel, false, false);
   size_t b = attend_workspace_bytes(q, kv, max_sel, true, false);
-  size_t bm = align256((size_t)q.B * kv.hkv * bitmap_words(q.W) * 4);
-  return (a > b ? a : b) + bm;
+  L.partials = kSyncRegionBytes;
+  L.partial_bytes = a > b ? a : b;
+  L.bitmap = L.partials + L.partial_bytes;
+  L.total = L.bitmap + align256((size_t)q.B * kv.hkv * bitmap_words(q.W) * 4);
+  return L;
 }
 
+size_t decode_ws(const QView& q, const KvView& kv, int max_sel) {
+  return decode_layout(q, kv, max_sel).total;
+}
+
+// Step workspace: [sync region][scores][selection][n][bitmap][gates][partials].
 struct StepLayout {
-  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, sync, attend, total;
+  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, attend, total;
 };
 
 StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense) {
   StepLayout L;
   const size_t bh = (size_t)q.B * kv.hkv;
-  size_t off = 0;
+  size_t off = kSyncRegionBytes;
   L.scores = off; off += align256(bh * q.W * 4);
   L.sel = off; off += align256(bh * max_sel * 4);
   L.n = off; off += align256(bh * 4);
@@ -140,7 +156,6 @@ StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recov
   L.cov_new = off; off += align256(bh * 4);
   L.acc_c = off; off += align256(bh);
   L.cov_c = off; off += align256(bh * 4);
-  L.sync = off; off += 256;
   L.attend = off; off += attend_workspace_bytes(q, kv, max_sel, recover, dense);
   L.total = off;
   return L;
@@ -292,8 +307,10 @@ int cvsa_sparse_decode(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   p.o_unnorm = o_unnorm;
   p.m_out = m;
   p.l_out = l;
-  p.workspace = workspace;
-  p.ws_bytes = workspace_bytes;
+  const DecodeLayout L = decode_layout(q, kv, max_sel);
+  p.partials = reinterpret_cast<uint8_t*>(workspace) + L.partials;
+  p.partial_bytes = L.partial_bytes;
+  p.head_done = ws_head_done(workspace);
   return cuda_status(launch_attend(q, kv, p, max_sel, (cudaStream_t)stream, false),
                      "decode launch");
 }
@@ -335,8 +352,8 @@ int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   const size_t need = decode_ws(q, kv, max_sel);
   if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
     return fail(CVSA_ERR_WORKSPACE, "workspace needs %zu bytes, 256-aligned", need);
-  const size_t bm_off = need - align256((size_t)q.B * kv.hkv * bitmap_words(q.W) * 4);
-  uint32_t* bitmap = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(workspace) + bm_off);
+  const DecodeLayout L = decode_layout(q, kv, max_sel);
+  uint32_t* bitmap = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(workspace) + L.bitmap);
   cudaStream_t s = (cudaStream_t)stream;
   st = cuda_status(launch_build_bitmap(page_indices, max_sel, n_per_head, q.B * kv.hkv, q.W, bitmap,
                                        bitmap_words(q.W), nullptr, s),
@@ -358,8 +375,9 @@ int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   p.ext_l = l_d;
   p.out = out;
   p.out_dtype = out_dtype;
-  p.workspace = workspace;
-  p.ws_bytes = workspace_bytes;
+  p.partials = reinterpret_cast<uint8_t*>(workspace) + L.partials;
+  p.partial_bytes = L.partial_bytes;
+  p.head_done = ws_head_done(workspace);
   return cuda_status(launch_attend(q, kv, p, max_sel, s, false), "recover launch");
 }
 
@@ -432,8 +450,9 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   ap.out_dtype = q.dtype;
   ap.counters = io->counters;
   ap.dev_err = io->dev_error;
-  ap.workspace = ws + L.attend;
-  ap.ws_bytes = workspace_bytes - L.attend;
+  ap.partials = ws + L.attend;
+  ap.partial_bytes = workspace_bytes - L.attend;
+  ap.head_done = ws_head_done(workspace);
 
   if (dense || mode == CVSA_MODE_REUSE) {
     ap.dense = dense;
@@ -441,11 +460,8 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
     ap.n0 = io->cached_n;
     ap.sel_stride = max_sel;
     ap.src_select = 0;
-    if (mode == CVSA_MODE_REUSE && io->step_flags) {
-      // reuse steps run no gate (backend.py:866-881)
-      st = cuda_status(cudaMemsetAsync(io->step_flags, 0, sizeof(int32_t), s), "flags");
-      if (st) return st;
-    }
+    // reuse and dense steps run no gate (backend.py:866-881): step_flags,
+    // accept and coverage keep the values of the last gated step
     if ((st = rec(CVSA_EV_ATTEND_BEGIN))) return st;
     st = cuda_status(launch_attend(q, kv, ap, max_sel, s, pdl), "attend launch");
     if (st) return st;
@@ -460,7 +476,7 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   float* cov_new = reinterpret_cast<float*>(ws + L.cov_new);
   uint8_t* acc_c = ws + L.acc_c;
   float* cov_c = reinterpret_cast<float*>(ws + L.cov_c);
-  int32_t* sync = reinterpret_cast<int32_t*>(ws + L.sync);  // [0..1] sync, [2] decision
+  int32_t* sync = ws_select_sync(workspace);  // [0..1] select tickets, [2] decision
 
   if ((st = rec(CVSA_EV_SCORE_BEGIN))) return st;
   st = cuda_status(launch_score_pages(q, kv, scores, io->dev_error, s, pdl), "score launch");

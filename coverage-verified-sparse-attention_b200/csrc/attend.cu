@@ -875,7 +875,6 @@ size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, boo
   size_t bytes = 0;
   bytes += grid * G * kv.d * 4;            // part_o
   bytes += grid * G * 2 * 4;               // part_ml
-  bytes += (size_t)q.B * kv.hkv * 4;       // head_done
   bytes = (bytes + 255) & ~size_t(255);
   return bytes;
 }
@@ -946,13 +945,14 @@ cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& 
   }
   const size_t grid = (size_t)q.B * kv.hkv * a.ic.iph;
   const int G = a.G;
-  uint8_t* ws = reinterpret_cast<uint8_t*>(p.workspace);
-  a.part_o = reinterpret_cast<float*>(ws);
+  a.part_o = reinterpret_cast<float*>(p.partials);
   a.part_ml = a.part_o + grid * G * kv.d;
-  a.head_done = reinterpret_cast<int32_t*>(a.part_ml + grid * G * 2);
+  a.head_done = p.head_done;
   a.scale = 1.0f / sqrtf((float)kv.d);
   if (grid == 0) return cudaSuccess;
   if (grid > 0x7fffffff) return cudaErrorInvalidValue;
+  if ((size_t)q.B * kv.hkv > (size_t)kMaxHeadsPerCall) return cudaErrorInvalidValue;
+  if (p.partial_bytes < grid * G * (kv.d + 2) * 4) return cudaErrorInvalidValue;
 
   if (mma) {
     if (kv.dtype == CVSA_DTYPE_BF16) {

@@ -35,6 +35,18 @@ struct QView {
 int num_sms();
 int dtype_bytes(int dtype);
 
+// Every workspace starts with a fixed region of counters that must be zero
+// when a kernel starts and that the kernels return to zero: per-(b, kv head)
+// tickets of the attention kernel, then the selection kernel's batch-global
+// words in its last 256 bytes. Its offset never depends on the call's
+// shapes, so calls of different shapes can share one workspace.
+constexpr size_t kSyncRegionBytes = 256 * 1024;
+constexpr int kMaxHeadsPerCall = (int)((kSyncRegionBytes - 256) / 4);  // batch * num_kv_heads
+inline int32_t* ws_head_done(void* ws) { return reinterpret_cast<int32_t*>(ws); }
+inline int32_t* ws_select_sync(void* ws) {
+  return reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(ws) + kSyncRegionBytes - 256);
+}
+
 // ---- score.cu ----
 cudaError_t launch_score_pages(const QView& q, const KvView& kv, float* scores,
                                int32_t* dev_err, cudaStream_t s, bool pdl);
@@ -115,9 +127,12 @@ struct AttendParams {
   uint8_t* accept_out; float* cov_out;
   const uint8_t* acc0; const float* cov0;
   const uint8_t* acc1; const float* cov1;
-  // workspace
-  void* workspace; size_t ws_bytes;
+  // scratch: item partials (attend_workspace_bytes) and the zero-initialised
+  // per-(b, h) tickets (ws_head_done of the call's workspace)
+  void* partials; size_t partial_bytes;
+  int32_t* head_done;
 };
+// Bytes of item-partial scratch (excluding the sync region).
 size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, bool recover,
                               bool dense);
 cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& p,

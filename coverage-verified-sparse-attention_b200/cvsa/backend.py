@@ -314,6 +314,8 @@ class CVSABackend:
             io.timing_events = ctypes.cast(self._timing_events, ctypes.c_void_p)
         elif self._track_timing:
             events = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NUM_EVENTS)]
+            for e in events:
+                e.record()      # torch creates the cudaEvent_t at its first record
             arr = (ctypes.c_void_p * _lib.NUM_EVENTS)(*[e.cuda_event for e in events])
             io.timing_events = ctypes.cast(arr, ctypes.c_void_p)
         _lib.check(lib.cvsa_decode_step(qd, kvd, cfg, io, ws.data_ptr(), ws.numel(), stream),

@@ -13,6 +13,11 @@
  *     stream). Every call only enqueues work on that stream; nothing blocks
  *     the host and nothing allocates memory: scratch comes from a
  *     caller-provided workspace whose size is queried with *_workspace_size.
+ *     A workspace is 256-byte aligned and zeroed once before its first use
+ *     (cvsa_workspace_reset). Its first 256 KiB hold counters the kernels
+ *     return to zero, at a fixed offset, so one workspace can serve calls of
+ *     any shapes in stream order; two calls that may run concurrently need
+ *     separate workspaces. batch * num_kv_heads is limited to 65472.
  *   - Integer tensors are int32 unless stated; layouts are row-major and
  *     contiguous unless a stride is passed.
  *   - Return value: CVSA_OK (0) or a negative CVSA_ERR_* status; the message
@@ -234,7 +239,9 @@ typedef struct cvsa_step_io {
   uint8_t* accept;         /* [batch, num_kv_heads] gate of the selection decoded, or NULL */
   float* coverage;         /* [batch, num_kv_heads] or NULL */
   int64_t* counters;       /* [CVSA_NUM_COUNTERS] accumulated, or NULL */
-  int32_t* step_flags;     /* [1]: bit0 every head accepted, bit1 rescored; or NULL */
+  int32_t* step_flags;     /* [1]: bit0 every head accepted, bit1 rescored; or NULL.
+                              REUSE and DENSE steps leave it (and accept/coverage)
+                              as the last gated step wrote them. */
   int32_t* dev_error;      /* [1]: CVSA_DEV_ERR_* bits OR-ed in, or NULL */
   /* Optional per-kernel timing (backend.py:225-250): NULL, or CVSA_NUM_EVENTS
    * cudaEvent_t handles recorded on `stream` around the scoring, selection/

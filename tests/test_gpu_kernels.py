@@ -240,4 +240,5 @@ def test_lse_merge_vs_reference_formula(cuda):
         assert (out.cpu() - ref).abs().max() < 1e-5
         out16 = selective_lse_merge(*(t.to(cuda) for t in (od, md, ld, oc, mc, lc, acc)), G,
                                     torch.bfloat16)
-        assert (out16.float().cpu() - ref).abs().max() < 1e-2
+        # one bf16 rounding of the same fp32 value: within the bf16 bar
+        assert ((out16.float().cpu() - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
