@@ -319,7 +319,8 @@ def run_cvsa(args, ws, rank, local):
             be2._timing_events = arr
             be2(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
             be2._timing_events = None
-            ev_sets.setdefault(be2._step, []).append((evs, arr))
+            lazy = be2._step % M_INTERVAL == 0
+            ev_sets.setdefault(lazy, []).append((evs, arr))
             be2.step_done(l, layers)
 
     be2 = make_backend()
@@ -330,17 +331,15 @@ def run_cvsa(args, ws, rank, local):
         step_events(be2)
     torch.cuda.synchronize()
     kern = {"score": [], "select": [], "attend_scoring": [], "attend_reuse": []}
-    for s, lst in ev_sets.items():
-        for evs, _ in lst:
-            e = evs
-            try:
+    for lazy, lst in ev_sets.items():
+        for e, _ in lst:
+            att = e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END])
+            if lazy:
                 kern["score"].append(e[_lib.EV_SCORE_BEGIN].elapsed_time(e[_lib.EV_SCORE_END]))
                 kern["select"].append(e[_lib.EV_SELECT_BEGIN].elapsed_time(e[_lib.EV_SELECT_END]))
-                kern["attend_scoring"].append(
-                    e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END]))
-            except (RuntimeError, ValueError):   # score/select pairs unrecorded: reuse step
-                kern["attend_reuse"].append(
-                    e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END]))
+                kern["attend_scoring"].append(att)
+            else:
+                kern["attend_reuse"].append(att)
     score_ms = statistics.mean(kern["score"]) if kern["score"] else None
     score_bytes = _scoring_pages(wls[0].context_lens, hkv) * KP_BYTES
     peak, peak_kind = _peaks()
