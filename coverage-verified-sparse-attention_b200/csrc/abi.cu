@@ -585,3 +585,103 @@ int cvsa_paged_gather(const cvsa_kv_desc_t* kvd, const int32_t* block_table_row,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free sparse decode.
+//
+// Some callers cannot allocate device memory at the point where they decode:
+// an inference server whose memory pool is fully reserved up front, a plugin
+// hosted by a runtime that owns every allocation, or a code path that must
+// not call cudaMalloc because it would synchronise the device. For them,
+// cvsa_sparse_decode_noalloc runs the same decode kernel as
+// cvsa_sparse_decode but takes its scratch (item partials and the per-head
+// tickets) from the array below, which is part of the library image: every
+// GPU that loads the library holds CVSA_NOALLOC_SCRATCH_BYTES of it until the
+// process exits.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CVSA_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// Device address of g_noalloc_scratch, looked up once per device (the name is
+// only a host-side stand-in for the symbol, not a device pointer).
+void* noalloc_scratch_ptr(int* status) {
+  static std::mutex mu;
+  static void* ptrs[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    *status = cuda_status(e, "cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    *status = fail(CVSA_ERR_UNSUPPORTED, "device ordinal %d above 63", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      *status = cuda_status(e == cudaSuccess ? cudaErrorInvalidSymbol : e,
+                            "cudaGetSymbolAddress(no-alloc scratch)");
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  *status = CVSA_OK;
+  return ptrs[dev];
+}
+
+}  // namespace
+
+extern "C" int cvsa_sparse_decode_noalloc(const cvsa_query_desc_t* qd,
+                                          const cvsa_kv_desc_t* kvd,
+                                          const int32_t* page_indices, int32_t max_sel,
+                                          const int32_t* n_per_head, float* o_unnorm, float* m,
+                                          float* l, void* out, int32_t out_dtype, void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (max_sel <= 0) return fail(CVSA_ERR_INVALID, "max_sel must be positive");
+  if (!attend_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "decode built for block_size 16, head_dim 64/128/256, G<=16");
+  if (out && !valid_dtype(out_dtype)) return fail(CVSA_ERR_INVALID, "out dtype unknown");
+  if (!out && !o_unnorm && !m && !l) return fail(CVSA_ERR_INVALID, "no output requested");
+  if (q.B == 0) return CVSA_OK;
+  if (!page_indices || !n_per_head) return fail(CVSA_ERR_INVALID, "NULL selection");
+  // scratch: [per-(b, h) tickets][item partials]
+  const size_t heads = (size_t)q.B * kv.hkv;
+  const size_t tickets = align256(heads * 4);
+  const size_t need = tickets + attend_workspace_bytes(q, kv, max_sel, false, false);
+  if (need > (size_t)CVSA_NOALLOC_SCRATCH_BYTES)
+    return fail(CVSA_ERR_UNSUPPORTED,
+                "decode needs %zu bytes of scratch; the no-alloc scratch holds %zu bytes "
+                "(use cvsa_sparse_decode with a caller workspace)",
+                need, (size_t)CVSA_NOALLOC_SCRATCH_BYTES);
+  uint8_t* base = static_cast<uint8_t*>(noalloc_scratch_ptr(&st));
+  if (!base) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  // The tickets must start at zero; a call that failed part-way could have left
+  // them set, so clear them on the stream before every launch.
+  st = cuda_status(cudaMemsetAsync(base, 0, heads * 4, s), "no-alloc scratch clear");
+  if (st) return st;
+  AttendParams p;
+  memset(&p, 0, sizeof(p));
+  p.sel0 = page_indices;
+  p.n0 = n_per_head;
+  p.sel_stride = max_sel;
+  p.src_select = 0;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.o_unnorm = o_unnorm;
+  p.m_out = m;
+  p.l_out = l;
+  p.head_done = reinterpret_cast<int32_t*>(base);
+  p.partials = base + tickets;
+  p.partial_bytes = (size_t)CVSA_NOALLOC_SCRATCH_BYTES - tickets;
+  return cuda_status(launch_attend(q, kv, p, max_sel, s, false), "no-alloc decode launch");
+}

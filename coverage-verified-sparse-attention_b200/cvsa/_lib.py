@@ -103,7 +103,10 @@ _SIGS = {
     "cvsa_paged_append": ([ctypes.POINTER(KvDesc), _P, _P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _P,
                            _P], ctypes.c_int),
     "cvsa_paged_gather": ([ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P, _P], ctypes.c_int),
+    "cvsa_sparse_decode_noalloc": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P,
+                                    _P, _P, _P, _P, _I, _P], ctypes.c_int),
 }
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _lib = None
 _lock = threading.Lock()

@@ -297,6 +297,33 @@ int cvsa_paged_gather(const cvsa_kv_desc_t* kv, const int32_t* block_table_row,
                       int32_t n_pages, void* k_out, void* v_out, int32_t* dev_error,
                       void* stream);
 
+/* ---- allocation-free decode ------------------------------------------ */
+
+/* Size of the library's built-in decode scratch (see below). */
+#define CVSA_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+/* The same sparse decode as cvsa_sparse_decode (same arguments and outputs),
+ * for callers that cannot allocate device memory where they decode -- e.g. a
+ * server whose memory pool is fully reserved at start-up, or a host runtime
+ * that owns every allocation -- and so cannot provide a workspace. Its
+ * scratch is a fixed array inside the library image
+ * (CVSA_NOALLOC_SCRATCH_BYTES on every GPU that loads the library, held until
+ * the process exits); it allocates nothing. This entry point has no
+ * counterpart in the reference.
+ *   - The first call on a device looks up that array's device address with
+ *     cudaGetSymbolAddress (the current device must be the one decoding);
+ *     make that first call before any stream capture.
+ *   - Shapes whose scratch would exceed CVSA_NOALLOC_SCRATCH_BYTES are
+ *     rejected with CVSA_ERR_UNSUPPORTED and a message naming both sizes.
+ *   - Every call on a device shares the one array, and each call clears the
+ *     part that must start at zero: two calls that can overlap on the GPU
+ *     (different streams without ordering between them) race and must not
+ *     be issued; calls ordered on one stream are safe. */
+int cvsa_sparse_decode_noalloc(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                               const int32_t* page_indices, int32_t max_sel,
+                               const int32_t* n_per_head, float* o_unnorm, float* m, float* l,
+                               void* out, int32_t out_dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
