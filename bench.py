@@ -247,6 +247,8 @@ def build_layers(dev, layers):
 
 
 def run_cvsa(args, ws, rank, local):
+    import ctypes
+
     from cvsa import _lib
     from cvsa.backend import CVSABackend
 
@@ -255,13 +257,14 @@ def run_cvsa(args, ws, rank, local):
     wls = build_layers(dev, layers)
     B, Hq, D = wls[0].q.shape
     hkv = wls[0].num_kv_heads
+    scoring_bytes_per_layer = [_scoring_pages(wl.context_lens, hkv) * KP_BYTES for wl in wls]
 
     def make_backend():
         return CVSABackend(hkv, Hq, D, 16, num_layers=layers, budget_pct=0.05,
                            coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
                            sink_pages=1, local_pages=2)
 
-    def step(be, qs=None, outs=None):
+    def eager_step(be, qs=None, outs=None):
         for l, wl in enumerate(wls):
             q = wl.q if qs is None else qs[l]
             o = be(q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
@@ -269,35 +272,56 @@ def run_cvsa(args, ws, rank, local):
                 outs[l] = o
             be.step_done(l, layers)
 
-    def timed(be, k, fn):
+    def alg_bytes(be, c0, lazy_steps):
+        c1 = be._counter_values()
+        pages = c1[_lib.CTR_PAGES_ATTENDED] - c0[_lib.CTR_PAGES_ATTENDED]
+        return pages * 2 * KP_BYTES + lazy_steps * sum(scoring_bytes_per_layer)
+
+    def timed(be, k, fn, lazy_steps):
         _barrier(ws)
         torch.cuda.synchronize()
         c0 = be._counter_values()
-        lazy_steps = sum(1 for s in range(be._step, be._step + k) if s % M_INTERVAL == 0)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(k):
-            fn()
+        for s in range(k):
+            fn(s)
         e1.record()
         torch.cuda.synchronize()
         _barrier(ws)
-        ms = e0.elapsed_time(e1)
-        c1 = be._counter_values()
-        pages = c1[_lib.CTR_PAGES_ATTENDED] - c0[_lib.CTR_PAGES_ATTENDED]
-        nbytes = pages * 2 * KP_BYTES + lazy_steps * sum(
-            _scoring_pages(wl.context_lens, hkv) for wl in wls) * KP_BYTES
-        return ms, nbytes, lazy_steps
+        return e0.elapsed_time(e1), alg_bytes(be, c0, lazy_steps)
 
-    # ---- device-resident timing (value) ----
-    be = make_backend()
     warm = args.warmup + ((-args.warmup) % M_INTERVAL)   # timed region starts a cycle
-    for _ in range(warm):
-        step(be)
+    lazy_steps = sum(1 for s in range(args.steps) if s % M_INTERVAL == 0)
+
+    # ---- device-resident timing (value): the step captured in CUDA graphs ----
+    # One graph for a lazy check step and one for a reuse step, each holding the
+    # 32 layer calls (3 kernels per layer on check steps, 1 on reuse steps).
+    be = make_backend()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs = {}
+    with torch.cuda.stream(side):
+        for _ in range(warm):
+            eager_step(be)
+        side.synchronize()
+        for kind, step_idx in (("lazy", 0), ("reuse", 1)):
+            g = torch.cuda.CUDAGraph()
+            be._step = step_idx
+            with torch.cuda.graph(g, stream=side):
+                for l, wl in enumerate(wls):
+                    be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+            graphs[kind] = g
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    for s in range(M_INTERVAL):                      # warm the graphs
+        graphs["lazy" if s % M_INTERVAL == 0 else "reuse"].replay()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
-    ms, nbytes, lazy_steps = timed(be, args.steps, lambda: step(be))
+    ms, nbytes = timed(be, args.steps,
+                       lambda s: graphs["lazy" if s % M_INTERVAL == 0 else "reuse"].replay(),
+                       lazy_steps)
     clk = clocks.stop()
     ms_max = _max_over_ranks(ms, ws)
     bytes_all = _sum_over_ranks(float(nbytes), ws)
@@ -306,52 +330,68 @@ def run_cvsa(args, ws, rank, local):
     launches = (lazy_steps * 3 + (args.steps - lazy_steps) * 1) * layers
     stats = be.get_stats()
 
-    # ---- per-kernel timing pass (events around each launch, same K steps) ----
-    ev_sets = {}
-
-    def step_events(be2):
-        for l, wl in enumerate(wls):
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NUM_EVENTS)]
-            for e in evs:
-                e.record()      # torch creates the cudaEvent_t at its first record
-            arr = (__import__("ctypes").c_void_p * _lib.NUM_EVENTS)(
-                *[e.cuda_event for e in evs])
-            be2._timing_events = arr
-            be2(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
-            be2._timing_events = None
-            lazy = be2._step % M_INTERVAL == 0
-            ev_sets.setdefault(lazy, []).append((evs, arr))
-            be2.step_done(l, layers)
-
-    be2 = make_backend()
-    for _ in range(warm):
-        step(be2)
-    torch.cuda.synchronize()
-    for _ in range(args.steps):
-        step_events(be2)
-    torch.cuda.synchronize()
+    # ---- per-kernel times: the same graphs captured with CUDA events ----
+    # around each launch (events between kernels disable launch overlap)
+    ev_graphs = {}
+    ev_sets = {"lazy": [], "reuse": []}
+    with torch.cuda.stream(side):
+        for kind, step_idx in (("lazy", 0), ("reuse", 1)):
+            g = torch.cuda.CUDAGraph()
+            be._step = step_idx
+            sets = []
+            for _ in wls:
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(_lib.NUM_EVENTS)]
+                for e in evs:
+                    e.record()       # torch creates the cudaEvent_t at its first record
+                sets.append((evs, (ctypes.c_void_p * _lib.NUM_EVENTS)(
+                    *[e.cuda_event for e in evs])))
+            side.synchronize()
+            with torch.cuda.graph(g, stream=side):
+                for l, wl in enumerate(wls):
+                    be._timing_events = sets[l][1]
+                    be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+                be._timing_events = None
+            ev_graphs[kind] = g
+            ev_sets[kind] = sets
+    torch.cuda.current_stream(dev).wait_stream(side)
     kern = {"score": [], "select": [], "attend_scoring": [], "attend_reuse": []}
-    for lazy, lst in ev_sets.items():
-        for e, _ in lst:
-            att = e[_lib.EV_ATTEND_BEGIN].elapsed_time(e[_lib.EV_ATTEND_END])
-            if lazy:
-                kern["score"].append(e[_lib.EV_SCORE_BEGIN].elapsed_time(e[_lib.EV_SCORE_END]))
-                kern["select"].append(e[_lib.EV_SELECT_BEGIN].elapsed_time(e[_lib.EV_SELECT_END]))
-                kern["attend_scoring"].append(att)
-            else:
-                kern["attend_reuse"].append(att)
+    for rep in range(2):
+        for kind in ("lazy", "reuse"):
+            ev_graphs[kind].replay()
+            torch.cuda.synchronize()
+            if rep == 0:
+                continue
+            for evs, _ in ev_sets[kind]:
+                att = evs[_lib.EV_ATTEND_BEGIN].elapsed_time(evs[_lib.EV_ATTEND_END])
+                if kind == "lazy":
+                    kern["score"].append(evs[_lib.EV_SCORE_BEGIN].elapsed_time(
+                        evs[_lib.EV_SCORE_END]))
+                    kern["select"].append(evs[_lib.EV_SELECT_BEGIN].elapsed_time(
+                        evs[_lib.EV_SELECT_END]))
+                    kern["attend_scoring"].append(att)
+                else:
+                    kern["attend_reuse"].append(att)
+    del ev_graphs
     score_ms = statistics.mean(kern["score"]) if kern["score"] else None
-    score_bytes = _scoring_pages(wls[0].context_lens, hkv) * KP_BYTES
+    score_bytes = scoring_bytes_per_layer[0]
     peak, peak_kind = _peaks()
     achieved = score_bytes / (score_ms * 1e-3) / 1e9 if score_ms else None
     traffic = None
-    tfile = os.path.join(ROOT, "profiles", "score_pages_config2_traffic.json")
+    tfile = os.path.join(ROOT, "profiles", "score_pages_config2.md")
     if os.path.exists(tfile):
-        with open(tfile) as f:
-            traffic = json.load(f).get("bytes_per_launch")
+        for line in open(tfile):
+            if line.startswith("traffic_bytes_per_launch:"):
+                traffic = int(line.split(":")[1])
     reuse_ms = statistics.mean(kern["attend_reuse"]) if kern["attend_reuse"] else None
     sel_pages = B * hkv * 28
     reuse_bytes = sel_pages * 2 * KP_BYTES
+
+    # ---- eager device-resident timing (one C-ABI call per layer, no graph) ----
+    be2 = make_backend()
+    for _ in range(warm):
+        eager_step(be2)
+    ms_eager, _ = timed(be2, args.steps, lambda s: eager_step(be2), lazy_steps)
+    ms_eager = _max_over_ranks(ms_eager, ws)
 
     # ---- end-to-end through the public API with host buffers ----
     be3 = make_backend()
@@ -359,7 +399,7 @@ def run_cvsa(args, ws, rank, local):
     out_host = [torch.empty_like(h).pin_memory() for h in q_host]
     q_dev = [torch.empty_like(wl.q) for wl in wls]
 
-    def e2e_step():
+    def e2e_step(_s=0):
         for l, wl in enumerate(wls):
             q_dev[l].copy_(q_host[l], non_blocking=True)
             o = be3(q_dev[l], wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
@@ -369,10 +409,11 @@ def run_cvsa(args, ws, rank, local):
     for _ in range(warm):
         e2e_step()
     torch.cuda.synchronize()
-    ms_e, nbytes_e, _ = timed(be3, args.steps, e2e_step)
+    ms_e, nbytes_e = timed(be3, args.steps, e2e_step, lazy_steps)
     ms_e = _max_over_ranks(ms_e, ws)
     e2e_val = _sum_over_ranks(float(nbytes_e), ws) / (ms_e * 1e-3) / 1e9
     h2d = sum(h.numel() * h.element_size() for h in q_host)
+    del graphs
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
@@ -397,9 +438,11 @@ def run_cvsa(args, ws, rank, local):
             "data": "synthetic (seeded N(0,1) + planted heavy pages; no checkpoints)",
             "config": {"workload": WORKLOAD, "batch_per_gpu": B, "ctx": 8192, "layers": layers,
                        "schedule": f"lazy M={M_INTERVAL}",
+                       "launch": "CUDA graph per step kind (lazy check / reuse), 32 layers each",
                        "l2": "inputs larger than L2 (1.07 GB K+V per layer, 32 pools)",
                        "parallelism": f"{ws} independent replicas (weak scaling)"},
             "us_per_layer": us_per_layer,
+            "eager_us_per_layer": ms_eager * 1e3 / (args.steps * layers),
             "tokens_per_s": B * ws * args.steps / (ms_max * 1e-3),
             "roofline": {"bound": "hbm", "kernel": "score_pages_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -419,7 +462,8 @@ def run_cvsa(args, ws, rank, local):
                                                  "total_scoring_steps", "total_coverage_checks")
                            if k in stats},
             "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": h2d, "ms_per_step": ms_e / args.steps},
+                    "d2h_bytes_per_step": h2d, "ms_per_step": ms_e / args.steps,
+                    "path": "CVSABackend.__call__ per layer (eager), pinned H2D q, D2H output"},
             "gpu_launches": launches,
             "clocks": clk,
         }

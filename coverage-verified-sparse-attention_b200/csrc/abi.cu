@@ -141,7 +141,8 @@ size_t decode_ws(const QView& q, const KvView& kv, int max_sel) {
 
 // Step workspace: [sync region][scores][selection][n][bitmap][gates][partials].
 struct StepLayout {
-  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, attend, total;
+  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, comp_cnt, comp_off, attend,
+      total;
 };
 
 StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense) {
@@ -156,6 +157,8 @@ StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recov
   L.cov_new = off; off += align256(bh * 4);
   L.acc_c = off; off += align256(bh);
   L.cov_c = off; off += align256(bh * 4);
+  L.comp_cnt = off; off += align256(bh * 4);
+  L.comp_off = off; off += align256((bh + 1) * 4);
   L.attend = off; off += attend_workspace_bytes(q, kv, max_sel, recover, dense);
   L.total = off;
   return L;
@@ -441,7 +444,11 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   const bool pdl = ev == nullptr;
   auto rec = [&](int i) -> int {
     if (!ev || !ev[i]) return CVSA_OK;
-    return cuda_status(cudaEventRecord((cudaEvent_t)ev[i], s), "event record");
+    // External: under stream capture the record becomes an event node of the
+    // graph (a plain record would only mark a dependency); outside capture it
+    // is an ordinary record.
+    return cuda_status(cudaEventRecordWithFlags((cudaEvent_t)ev[i], s, cudaEventRecordExternal),
+                       "event record");
   };
 
   AttendParams ap;
@@ -514,6 +521,13 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   sp.has_cache = cfg->has_cache;
   sp.lazy_stats = cfg->lazy_stats;
   sp.step_flags = io->step_flags;
+  int32_t* comp_cnt = reinterpret_cast<int32_t*>(ws + L.comp_cnt);
+  int32_t* comp_off = reinterpret_cast<int32_t*>(ws + L.comp_off);
+  if (recover) {
+    sp.comp_cnt = comp_cnt;
+    sp.comp_off = comp_off;
+    sp.comp_chunk = attend_complement_chunk();
+  }
   if ((st = rec(CVSA_EV_SELECT_BEGIN))) return st;
   st = cuda_status(launch_select_gate(sp, s, pdl), "select launch");
   if (st) return st;
@@ -527,6 +541,7 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   ap.src_select = (mode == CVSA_MODE_LAZY) ? 2 : 1;
   ap.decision = sync + 2;
   ap.recover = recover;
+  ap.comp_off = recover ? comp_off : nullptr;
   ap.accept = acc_new;
   ap.bitmap = bitmap;
   ap.bitmap_words = bitmap_words(q.W);

@@ -10,23 +10,28 @@
 //     that list; here selected pages are skipped through a bitmap), merged
 //     with the draft by cvsa/kernels/coverage.py:274-326.
 //
-// Work decomposition. For every (b, kv head) there are `nd` draft items
-// (chunks of the selection list) and `nc` complement items (chunks of the
-// logical page range, minus selected pages) -- or, for dense layers, `nc`
-// chunks of all valid pages. One CTA of 4 warps runs one item; inactive items
-// (accepted heads' complement chunks, chunks past the end) exit at once. The
-// 4 warps take the item's pages round robin; each warp streams its pages
-// through its own 3-stage shared-memory ring filled by TMA (one box per
-// 64-wide slice of head_dim for K and for V, 128-byte swizzle) and keeps its
-// own online-softmax state. All G query heads of the KV head are packed into
-// the M dimension of mma.sync m16n8k16 (bf16/f16 in, f32 accumulate):
-// S = Q K^T (M = query heads, N = 16 tokens, K = head_dim) and O += P V
-// (K = 16 tokens, N = head_dim); P goes from the S accumulators to the A
-// operand in registers. The warps' states are merged in shared memory into an
-// item partial (o, m, l) per query head; the last CTA of (b, h) to finish
-// (atomic ticket, no spin) merges the item partials in a fixed order, so the
-// result is deterministic, and writes the output. fp32 (and mixed-dtype)
-// KV use a CUDA-core variant of the per-page step with the same framework.
+// Work decomposition. Each (b, kv head) has `nd` draft items (chunks of up to
+// 32 pages of its selection) and, when it must recover, complement items
+// (chunks of 32 logical pages minus the selected ones); a dense layer has
+// chunks of all valid pages. Draft items are enumerated statically; the
+// complement items of the rejected heads form a compact list whose per-head
+// offsets the selection kernel's last CTA scanned, so CTAs never wait on heads
+// that accepted. CTAs are persistent (2 per SM) and walk this item space with a
+// grid stride. A CTA of 4 warps runs one item at a time: the warps take its
+// pages round robin, each streaming them through its own 3-stage shared
+// memory ring filled by TMA (one box per 64-wide slice of head_dim for K and
+// for V, 128-byte swizzle; ring phases carry over from item to item), and each
+// keeps an online-softmax state. All G query heads of the KV head are packed
+// into the M dimension of mma.sync m16n8k16 (bf16/f16 in, f32 accumulate):
+// S = Q K^T (M = query heads, N = 16 tokens, K = head_dim, two independent
+// accumulation chains) and O += P V (K = 16 tokens, N = head_dim), with P
+// passed from the S accumulators to the A operand in registers. Warp states
+// merge in shared memory into an item partial (o, m, l) per query head. A head
+// with one item is finished by that CTA; otherwise the last CTA to finish an
+// item of the head (atomic ticket, no spin) merges the partials in a fixed
+// order -- draft chunks, then complement chunks -- so results are
+// deterministic. fp32 (and mixed-dtype) KV use a CUDA-core per-page step in the
+// same framework.
 #include <mutex>
 #include <unordered_map>
 
@@ -38,14 +43,14 @@ namespace cvsa {
 namespace {
 
 constexpr int kNW = 4;             // warps per CTA
-constexpr int kStages = 3;         // per-warp TMA ring depth
+constexpr int kStages = 2;         // per-warp TMA ring depth (3 CTAs fit per SM)
 constexpr int kMaxItemPages = 32;  // pages per item (list capacity)
 constexpr int kBS = 16;            // tokens per page (kernels built for 16)
 
 struct ItemCfg {
   int cd, nd;  // draft chunk pages, draft items per head
   int cc, nc;  // complement/dense chunk pages, items per head
-  int iph;     // nd + nc
+  int iph;     // scratch slots per head (nd + nc)
 };
 
 struct AttendArgs {
@@ -69,6 +74,7 @@ struct AttendArgs {
   const uint8_t* accept;
   const uint32_t* bitmap;
   int bitmap_words;
+  const int32_t* comp_off;  // [heads + 1] complement-item offsets, or null (static list)
   int external_draft;
   const float* ext_o;
   const float* ext_m;
@@ -89,10 +95,11 @@ struct AttendArgs {
   const float* cov0;
   const uint8_t* acc1;
   const float* cov1;
-  float* part_o;   // [grid][G][D]
-  float* part_ml;  // [grid][G][2]
+  float* part_o;   // [heads * iph][G][D]
+  float* part_ml;  // [heads * iph][G][2]
   int32_t* head_done;
   ItemCfg ic;
+  int heads;       // B * hkv
   float scale;
 };
 
@@ -100,24 +107,32 @@ struct AttendArgs {
 // per-item bookkeeping shared by both per-page variants
 // ---------------------------------------------------------------------------
 struct ItemInfo {
-  int bh, b, h, j;
+  int bh, b, h;
   int ctx, nv;
   int src;  // 0/1 selection source, -1 dense
   int n_sel;
   const int32_t* sel;
   bool rec;
   int nd_act, nc_act, expected;
-  int role;  // 0 draft/dense, 1 complement
+  int role;   // 0 draft/dense chunk, 1 complement chunk
+  int chunk;  // chunk index within its role
+  int slot;   // scratch slot of this item
   bool active;
 };
 
-__device__ __forceinline__ ItemInfo item_info(const AttendArgs& a) {
+__device__ __forceinline__ int item_source(const AttendArgs& a) {
+  int s = a.src_select;
+  if (s == 2) s = (a.decision[0] & 1) ? 0 : 1;
+  return s;
+}
+
+__device__ __forceinline__ ItemInfo make_item(const AttendArgs& a, int bh, int role, int chunk) {
   ItemInfo it;
-  const int item = blockIdx.x;
-  it.bh = item / a.ic.iph;
-  it.j = item % a.ic.iph;
-  it.b = it.bh / a.hkv;
-  it.h = it.bh % a.hkv;
+  it.bh = bh;
+  it.b = bh / a.hkv;
+  it.h = bh % a.hkv;
+  it.role = role;
+  it.chunk = chunk;
   it.ctx = a.lens[it.b];
   it.nv = min(n_valid_pages(it.ctx, kBS), a.W);
   if (a.dense) {
@@ -125,13 +140,12 @@ __device__ __forceinline__ ItemInfo item_info(const AttendArgs& a) {
     it.n_sel = 0;
     it.sel = nullptr;
   } else {
-    int s = a.src_select;
-    if (s == 2) s = (a.decision[0] & 1) ? 0 : 1;
+    const int s = item_source(a);
     it.src = s;
-    it.sel = (s ? a.sel1 : a.sel0) + (int64_t)it.bh * a.sel_stride;
-    it.n_sel = min(max((s ? a.n1 : a.n0)[it.bh], 0), a.sel_stride);
+    it.sel = (s ? a.sel1 : a.sel0) + (int64_t)bh * a.sel_stride;
+    it.n_sel = min(max((s ? a.n1 : a.n0)[bh], 0), a.sel_stride);
   }
-  it.rec = a.recover && !a.dense && (a.external_draft || it.src == 1) && a.accept[it.bh] == 0;
+  it.rec = a.recover && !a.dense && (a.external_draft || it.src == 1) && a.accept[bh] == 0;
   const int nvc = (it.nv + a.ic.cc - 1) / a.ic.cc;
   if (a.dense) {
     it.nd_act = 0;
@@ -144,35 +158,69 @@ __device__ __forceinline__ ItemInfo item_info(const AttendArgs& a) {
     it.nc_act = it.rec ? max(1, nvc) : 0;
   }
   it.expected = it.nd_act + it.nc_act;
-  if (it.j < a.ic.nd) {
-    it.role = 0;
-    it.active = it.j < it.nd_act;
+  if (role == 0 && !a.dense) {
+    it.active = chunk < it.nd_act;
+    it.slot = bh * a.ic.iph + chunk;
   } else {
-    it.role = a.dense ? 0 : 1;
-    it.active = (it.j - a.ic.nd) < it.nc_act;
+    it.active = chunk < it.nc_act;
+    it.slot = bh * a.ic.iph + a.ic.nd + chunk;
   }
   return it;
 }
 
-// Build this item's page list (ascending within the item) in shared memory.
+// Virtual item space: [0, n_static) draft (or dense) chunks of every head,
+// then complement chunks: a compact list when comp_off is given, else every
+// head's chunks (inactive ones skipped).
+__device__ __forceinline__ int n_static_items(const AttendArgs& a) {
+  return a.heads * (a.dense ? a.ic.nc : a.ic.nd);
+}
+
+__device__ __forceinline__ int n_total_items(const AttendArgs& a) {
+  const int ns = n_static_items(a);
+  if (a.dense || !a.recover) return ns;
+  if (a.comp_off) return ns + a.comp_off[a.heads];
+  return ns + a.heads * a.ic.nc;
+}
+
+__device__ __forceinline__ ItemInfo decode_item(const AttendArgs& a, int v) {
+  const int ns = n_static_items(a);
+  if (v < ns) {
+    const int per = a.dense ? a.ic.nc : a.ic.nd;
+    return make_item(a, v / per, a.dense ? 0 : 0, v % per);
+  }
+  const int u = v - ns;
+  if (a.comp_off) {
+    // largest bh with comp_off[bh] <= u
+    int lo = 0, hi = a.heads - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.comp_off[mid] <= u) lo = mid;
+      else hi = mid - 1;
+    }
+    return make_item(a, lo, 1, u - a.comp_off[lo]);
+  }
+  return make_item(a, u / a.ic.nc, 1, u % a.ic.nc);
+}
+
+// Build this item's page list (ascending within the item) in shared memory,
+// with each page's physical block resolved once here (-1 when the block-table
+// entry lies outside the pool), so the page loop never waits on the table.
 __device__ __forceinline__ void build_page_list(const AttendArgs& a, const ItemInfo& it,
-                                                int* list, int* cnt) {
+                                                int* list, int* blist, int* cnt) {
   if (threadIdx.x >= 32) return;
   const int lane = threadIdx.x;
   int pg = -1;
   bool keep = false;
-  if (it.j < a.ic.nd) {
-    const int i0 = it.j * a.ic.cd;
-    const int i = i0 + lane;
+  if (it.role == 0 && !a.dense) {
+    const int i = it.chunk * a.ic.cd + lane;
     if (lane < a.ic.cd && i < it.n_sel) {
       pg = it.sel[i];
       keep = pg >= 0 && pg < a.W;
       if (!keep) set_dev_error(a.dev_err, CVSA_DEV_ERR_PAGE_RANGE);
     }
   } else {
-    const int c = it.j - a.ic.nd;
     const bool empty = a.external_draft && !it.rec;
-    const int p = c * a.ic.cc + lane;
+    const int p = it.chunk * a.ic.cc + lane;
     if (!empty && lane < a.ic.cc && p < it.nv) {
       pg = p;
       keep = true;
@@ -183,7 +231,16 @@ __device__ __forceinline__ void build_page_list(const AttendArgs& a, const ItemI
     }
   }
   const uint32_t m = __ballot_sync(0xffffffffu, keep);
-  if (keep) list[__popc(m & ((1u << lane) - 1u))] = pg;
+  if (keep) {
+    int blk = a.tables[(int64_t)it.b * a.W + pg];
+    if (blk < 0 || blk >= a.num_blocks) {
+      set_dev_error(a.dev_err, CVSA_DEV_ERR_BLOCK_RANGE);
+      blk = -1;
+    }
+    const int pos = __popc(m & ((1u << lane) - 1u));
+    list[pos] = pg;
+    blist[pos] = blk;
+  }
   if (lane == 0) *cnt = __popc(m);
 }
 
@@ -215,14 +272,54 @@ __device__ __forceinline__ void store_out_dt(void* out, int dt, int64_t idx, flo
   else store_out<float>(out, idx, v);
 }
 
-// Final merge for one (b, h): combine role-0 partials into the draft
-// (o_d, m_d, l_d), role-1 partials into the complement, then write outputs.
-// `ip_*` is this CTA's own item partial (used when it is the only item).
+// Final merge of one (b, h). `single`: the head has one item whose partial is
+// ip_o/ip_ml (shared memory). Otherwise the partials of every item of the head
+// are in part_o/part_ml; their (m, l) are staged in `stage` (shared, at least
+// n_items * G * 2 floats when `fits`) and each output element sums its item
+// partials with independent loads.
 template <int D>
 __device__ void finalize_head(const AttendArgs& a, const ItemInfo& it, const float* ip_o,
-                              const float* ip_ml, bool single) {
+                              const float* ip_ml, bool single, float* stage, int stage_floats) {
   const int G = a.G;
-  const int64_t item_base = (int64_t)it.bh * a.ic.iph;
+  const int n0 = a.external_draft ? 0 : (a.dense ? it.nc_act : it.nd_act);
+  const int off0 = a.dense ? a.ic.nd : 0;   // first slot of the role-0 items
+  const int n1 = it.rec ? it.nc_act : 0;
+  const int nitems = n0 + n1;
+  const int64_t base = (int64_t)it.bh * a.ic.iph;
+  // slot of item i of the combined list: role-0 items, then role-1 items
+  auto slot_of = [&](int i) -> int64_t {
+    return base + (i < n0 ? off0 + i : a.ic.nd + (i - n0));
+  };
+  const bool staged = !single && nitems * G * 2 + 4 * G <= stage_floats;
+  if (staged) {
+    // stage (m, l) of every item; then per (role, g): M, weights, L
+    float* w = stage;                       // [nitems][G] weights (m replaced)
+    float* lsum = stage + nitems * G;       // [nitems][G] l
+    float* red = stage + 2 * nitems * G;    // [2][G][2]: M, L per role
+    for (int e = threadIdx.x; e < nitems * G; e += kNW * 32) {
+      const int i = e / G, g = e % G;
+      const int64_t s = slot_of(i);
+      w[e] = __ldcg(&a.part_ml[(s * G + g) * 2]);
+      lsum[e] = __ldcg(&a.part_ml[(s * G + g) * 2 + 1]);
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * G) {
+      const int r = threadIdx.x / G, g = threadIdx.x % G;
+      const int i0 = r == 0 ? 0 : n0, i1 = r == 0 ? n0 : nitems;
+      float M = neg_inf();
+      for (int i = i0; i < i1; ++i) M = fmaxf(M, w[i * G + g]);
+      float L = 0.f;
+      for (int i = i0; i < i1; ++i) {
+        const float mi = w[i * G + g];
+        const float wi = (mi == neg_inf()) ? 0.f : expf(mi - M);
+        w[i * G + g] = wi;
+        L += lsum[i * G + g] * wi;
+      }
+      red[(r * G + g) * 2] = M;
+      red[(r * G + g) * 2 + 1] = L;
+    }
+    __syncthreads();
+  }
   for (int e = threadIdx.x; e < G * D; e += kNW * 32) {
     const int g = e / D, d = e % D;
     float md = neg_inf(), ld = 0.f, od = 0.f;
@@ -231,23 +328,30 @@ __device__ void finalize_head(const AttendArgs& a, const ItemInfo& it, const flo
       const float pm = ip_ml[g * 2], pl = ip_ml[g * 2 + 1], po = ip_o[g * D + d];
       if (it.role == 0) { md = pm; ld = pl; od = po; }
       else { mc = pm; lc = pl; oc = po; }
+    } else if (staged) {
+      const float* w = stage;
+      const float* red = stage + 2 * nitems * G;
+      md = red[g * 2];
+      ld = red[g * 2 + 1];
+      mc = red[(G + g) * 2];
+      lc = red[(G + g) * 2 + 1];
+      float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+      for (int i = 0; i < n0; ++i)
+        acc0 += w[i * G + g] * __ldcg(&a.part_o[(slot_of(i) * G + g) * D + d]);
+#pragma unroll 4
+      for (int i = n0; i < nitems; ++i)
+        acc1 += w[i * G + g] * __ldcg(&a.part_o[(slot_of(i) * G + g) * D + d]);
+      od = acc0;
+      oc = acc1;
     } else {
-      // role 0 items
-      if (!a.external_draft) {
-        const int n0 = a.dense ? it.nc_act : it.nd_act;
-        const int off0 = a.dense ? a.ic.nd : 0;
-        for (int i = 0; i < n0; ++i) {
-          const int64_t itm = item_base + off0 + i;
-          lse_combine(md, ld, od, a.part_ml[(itm * G + g) * 2], a.part_ml[(itm * G + g) * 2 + 1],
-                      a.part_o[(itm * G + g) * D + d]);
-        }
-      }
-      if (it.rec) {
-        for (int i = 0; i < it.nc_act; ++i) {
-          const int64_t itm = item_base + a.ic.nd + i;
-          lse_combine(mc, lc, oc, a.part_ml[(itm * G + g) * 2], a.part_ml[(itm * G + g) * 2 + 1],
-                      a.part_o[(itm * G + g) * D + d]);
-        }
+      for (int i = 0; i < nitems; ++i) {
+        const int64_t s = slot_of(i);
+        const float pm = __ldcg(&a.part_ml[(s * G + g) * 2]);
+        const float pl = __ldcg(&a.part_ml[(s * G + g) * 2 + 1]);
+        const float po = __ldcg(&a.part_o[(s * G + g) * D + d]);
+        if (i < n0) lse_combine(md, ld, od, pm, pl, po);
+        else lse_combine(mc, lc, oc, pm, pl, po);
       }
     }
     const int64_t qrow = (int64_t)it.b * a.hq + (int64_t)it.h * G + g;
@@ -299,23 +403,42 @@ __device__ void finalize_head(const AttendArgs& a, const ItemInfo& it, const flo
   }
 }
 
-// Merge the kNW warp states (wb_o [kNW][GP][D], wb_ml [kNW][GP][2]) into the
-// item partial ip_o [G][D], ip_ml [G][2].
+// Row stride (floats) of the warp-state buffer: D + 8 keeps the 8 query rows a
+// warp writes at once in distinct shared-memory banks.
 template <int D>
-__device__ void merge_warps(int G, int GP, const float* wb_o, const float* wb_ml, float* ip_o,
+constexpr int wb_stride() { return D + 8; }
+
+// Merge the kNW warp states (wb_o [kNW][GP][D + 8], wb_ml [kNW][GP][2]) into
+// the item partial ip_o [G][D], ip_ml [G][2].
+template <int D>
+__device__ void merge_warps(int G, int GP, const float* wb_o, float* wb_ml, float* ip_o,
                             float* ip_ml) {
+  constexpr int S = wb_stride<D>();
+  // per query row: the merged (m, l) and each warp's weight exp(m_w - m),
+  // computed once; the weights overwrite the warps' m in wb_ml
+  if (threadIdx.x < G) {
+    const int g = threadIdx.x;
+    float m = neg_inf();
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) m = fmaxf(m, wb_ml[(w * GP + g) * 2]);
+    float l = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNW; ++w) {
+      const float mw = wb_ml[(w * GP + g) * 2];
+      const float sw = (mw == neg_inf()) ? 0.f : expf(mw - m);
+      wb_ml[(w * GP + g) * 2] = sw;
+      l += wb_ml[(w * GP + g) * 2 + 1] * sw;
+    }
+    ip_ml[g * 2] = m;
+    ip_ml[g * 2 + 1] = l;
+  }
+  __syncthreads();
   for (int e = threadIdx.x; e < G * D; e += kNW * 32) {
     const int g = e / D, d = e % D;
-    float m = neg_inf(), l = 0.f, o = 0.f;
+    float o = 0.f;
 #pragma unroll
-    for (int w = 0; w < kNW; ++w)
-      lse_combine(m, l, o, wb_ml[(w * GP + g) * 2], wb_ml[(w * GP + g) * 2 + 1],
-                  wb_o[(w * GP + g) * D + d]);
+    for (int w = 0; w < kNW; ++w) o += wb_ml[(w * GP + g) * 2] * wb_o[(w * GP + g) * S + d];
     ip_o[g * D + d] = o;
-    if (d == 0) {
-      ip_ml[g * 2] = m;
-      ip_ml[g * 2 + 1] = l;
-    }
   }
 }
 
@@ -330,17 +453,16 @@ struct MmaPath {
   static constexpr int kGP = 8 * GR;                  // query rows per warp state
   static constexpr int kNT = D / 8;                   // n-tiles of O
 
-  static constexpr size_t smem_bytes() {
-    // stage ring (reused afterwards for the warp-state merge) + item partial
-    // + barriers + page list + 1 KB alignment slack
+  static constexpr size_t ring_bytes() {
     size_t ring = (size_t)kNW * kStages * kStageBytes;
-    size_t wb = (size_t)kNW * kGP * D * 4 + (size_t)kNW * kGP * 2 * 4;
-    size_t r = ring > wb ? ring : wb;
-    return 1024 + r + (size_t)16 * D * 4 + 16 * 2 * 4 + kNW * kStages * 8 + (kMaxItemPages + 4) * 4;
+    size_t wb = (size_t)kNW * kGP * wb_stride<D>() * 4 + (size_t)kNW * kGP * 2 * 4;
+    return ring > wb ? ring : wb;
   }
 
-  __device__ static void run(const AttendArgs& a, const ItemInfo& it, uint8_t* ring, uint64_t* bars,
-                             const int* list, int cnt, float* wb_o, float* wb_ml) {
+  // Returns false if a copy never arrived (the warp drained what it could).
+  __device__ static bool run(const AttendArgs& a, const ItemInfo& it, uint8_t* ring,
+                             uint64_t* bars, const int* list, const int* blist, int cnt,
+                             float* wb_o, float* wb_ml, uint32_t& gpage) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gq = lane >> 2, tq = lane & 3;
     const int G = a.G;
@@ -381,16 +503,11 @@ struct MmaPath {
     const int nmine = cnt > w ? (cnt - w + kNW - 1) / kNW : 0;
     uint8_t* my_ring = ring + (size_t)w * kStages * kStageBytes;
     uint64_t* my_bar = bars + w * kStages;
-    const int32_t* trow = a.tables + (int64_t)it.b * a.W;
 
-    auto page_blk = [&](int jj) {
-      const int pg = list[w + jj * kNW];
-      const int blk = trow[pg];
-      return (blk >= 0 && blk < a.num_blocks) ? blk : -1;
-    };
+    auto page_blk = [&](int jj) { return blist[w + jj * kNW]; };
     auto issue = [&](int jj) {
       if (lane == 0) {
-        const int st = jj % kStages;
+        const int st = (int)((gpage + jj) % kStages);
         const int blk = page_blk(jj);
         uint8_t* dst = my_ring + (size_t)st * kStageBytes;
         if (blk >= 0) {
@@ -401,25 +518,28 @@ struct MmaPath {
             tma_load_4d(dst + (kSub + s) * kTileBytes, &a.vmap, &my_bar[st], s * 64, it.h, 0, blk);
           }
         } else {
-          set_dev_error(a.dev_err, CVSA_DEV_ERR_BLOCK_RANGE);
-          mbar_arrive_expect_tx(&my_bar[st], 0);
+          mbar_arrive_expect_tx(&my_bar[st], 0);  // out-of-pool block: nothing to load
         }
       }
     };
 
+    // the ring (or the warp-state buffer aliasing it) was last read before the
+    // CTA barrier that precedes this call; order those reads before the copies
+    fence_proxy_async_smem();
     const int npro = nmine < kStages ? nmine : kStages;
     for (int jj = 0; jj < npro; ++jj) issue(jj);
 
     bool failed = false;
     for (int jj = 0; jj < nmine; ++jj) {
-      const int st = jj % kStages;
-      const uint32_t ph = (jj / kStages) & 1;
+      const uint32_t gp = gpage + jj;
+      const int st = (int)(gp % kStages);
+      const uint32_t ph = (gp / kStages) & 1;
       if (!mbar_wait_bounded(&my_bar[st], ph)) {
         failed = true;
         set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
         // drain the copies still in flight for this warp (bounded), then stop
         for (int k2 = jj + 1; k2 < nmine && k2 < jj + kStages; ++k2)
-          mbar_wait_bounded(&my_bar[k2 % kStages], (k2 / kStages) & 1);
+          mbar_wait_bounded(&my_bar[(gpage + k2) % kStages], ((gpage + k2) / kStages) & 1);
         break;
       }
       const int pg = list[w + jj * kNW];
@@ -428,12 +548,15 @@ struct MmaPath {
       if (ntok > 0) {
         const uint32_t kbase = smem_u32(my_ring + (size_t)st * kStageBytes);
         const uint32_t vbase = kbase + kSub * kTileBytes;
-        // ---- S = Q K^T over the 16 tokens of the page ----
-        float s[2][4];
+        // ---- S = Q K^T over the 16 tokens, two independent k-chains ----
+        float s[2][4], s2[2][4];
 #pragma unroll
         for (int n = 0; n < 2; ++n)
 #pragma unroll
-          for (int r = 0; r < 4; ++r) s[n][r] = 0.f;
+          for (int r = 0; r < 4; ++r) {
+            s[n][r] = 0.f;
+            s2[n][r] = 0.f;
+          }
         {
           const int tok = (lane & 7) + ((lane >> 4) & 1) * 8;
           const int chsel = (lane >> 3) & 1;
@@ -449,9 +572,18 @@ struct MmaPath {
             afr[1] = GR == 2 ? qa[ks][1] : 0u;
             afr[2] = qa[ks][GR];
             afr[3] = GR == 2 ? qa[ks][GR + 1] : 0u;
-            Mma<T>::m16n8k16(s[0], afr, b0, b1);
-            Mma<T>::m16n8k16(s[1], afr, b2, b3);
+            if (ks & 1) {
+              Mma<T>::m16n8k16(s2[0], afr, b0, b1);
+              Mma<T>::m16n8k16(s2[1], afr, b2, b3);
+            } else {
+              Mma<T>::m16n8k16(s[0], afr, b0, b1);
+              Mma<T>::m16n8k16(s[1], afr, b2, b3);
+            }
           }
+#pragma unroll
+          for (int n = 0; n < 2; ++n)
+#pragma unroll
+            for (int r = 0; r < 4; ++r) s[n][r] += s2[n][r];
         }
         // ---- online softmax per query row ----
         float pv[2][4];
@@ -517,14 +649,9 @@ struct MmaPath {
               Mma<T>::m16n8k16(o[nt], pa, b0, b1);
               Mma<T>::m16n8k16(o[nt + 1], pa, b2, b3);
             } else {
-              float c0[4] = {o[nt][0], o[nt][1], dummy[0], dummy[1]};
-              Mma<T>::m16n8k16(c0, pa, b0, b1);
-              o[nt][0] = c0[0];
-              o[nt][1] = c0[1];
-              float c1[4] = {o[nt + 1][0], o[nt + 1][1], dummy[0], dummy[1]};
-              Mma<T>::m16n8k16(c1, pa, b2, b3);
-              o[nt + 1][0] = c1[0];
-              o[nt + 1][1] = c1[1];
+              // rows 8..15 are padding: accumulate them into scratch registers
+              Mma<T>::m16n8k16(o[nt][0], o[nt][1], dummy[0], dummy[1], pa, b0, b1);
+              Mma<T>::m16n8k16(o[nt + 1][0], o[nt + 1][1], dummy[0], dummy[1], pa, b2, b3);
             }
           }
         }
@@ -535,6 +662,7 @@ struct MmaPath {
         issue(jj + kStages);
       }
     }
+    gpage += nmine;
     if (failed) {
 #pragma unroll
       for (int r = 0; r < GR; ++r) {
@@ -544,19 +672,21 @@ struct MmaPath {
     }
     // The ring is reused as the warp-state buffer: wait for every warp.
     __syncthreads();
+    constexpr int S = wb_stride<D>();
 #pragma unroll
     for (int r = 0; r < GR; ++r) {
       const int g = gq + 8 * r;
 #pragma unroll
       for (int n = 0; n < kNT; ++n) {
-        wb_o[(w * kGP + g) * D + n * 8 + tq * 2] = failed ? 0.f : o[n][2 * r];
-        wb_o[(w * kGP + g) * D + n * 8 + tq * 2 + 1] = failed ? 0.f : o[n][2 * r + 1];
+        float2 v2 = failed ? make_float2(0.f, 0.f) : make_float2(o[n][2 * r], o[n][2 * r + 1]);
+        *reinterpret_cast<float2*>(&wb_o[(w * kGP + g) * S + n * 8 + tq * 2]) = v2;
       }
       if (tq == 0) {
         wb_ml[(w * kGP + g) * 2] = m_run[r];
         wb_ml[(w * kGP + g) * 2 + 1] = l_run[r];
       }
     }
+    return !failed;
   }
 };
 
@@ -568,12 +698,14 @@ template <typename T, typename TQ, int D, int GM>
 struct SimtPath {
   static constexpr int kGP = GM;
   static constexpr int kPer = D / 32;
-  static constexpr size_t smem_bytes() {
-    size_t wb = (size_t)kNW * GM * D * 4 + (size_t)kNW * GM * 2 * 4;
-    return 1024 + wb + (size_t)16 * D * 4 + 16 * 2 * 4 + kNW * kStages * 8 + (kMaxItemPages + 4) * 4;
+  static constexpr size_t ring_bytes() {
+    // warp-state buffer; at least 64 KB so the finaliser can stage partials
+    size_t wb = (size_t)kNW * GM * wb_stride<D>() * 4 + (size_t)kNW * GM * 2 * 4;
+    return wb > 65536 ? wb : 65536;
   }
-  __device__ static void run(const AttendArgs& a, const ItemInfo& it, uint8_t*, uint64_t*,
-                             const int* list, int cnt, float* wb_o, float* wb_ml) {
+  __device__ static bool run(const AttendArgs& a, const ItemInfo& it, uint8_t*, uint64_t*,
+                             const int* list, const int* blist, int cnt, float* wb_o,
+                             float* wb_ml, uint32_t&) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = a.G;
     float qv[GM][kPer];
@@ -594,14 +726,10 @@ struct SimtPath {
     }
     const T* K = reinterpret_cast<const T*>(a.k);
     const T* V = reinterpret_cast<const T*>(a.v);
-    const int32_t* trow = a.tables + (int64_t)it.b * a.W;
     for (int jj = w; jj < cnt; jj += kNW) {
       const int pg = list[jj];
-      const int blk = trow[pg];
-      if (blk < 0 || blk >= a.num_blocks) {
-        if (lane == 0) set_dev_error(a.dev_err, CVSA_DEV_ERR_BLOCK_RANGE);
-        continue;
-      }
+      const int blk = blist[jj];
+      if (blk < 0) continue;  // out-of-pool block (recorded when the list was built)
       const int ntok = min(kBS, it.ctx - pg * kBS);
       for (int t = 0; t < ntok; ++t) {
         const int64_t base = (int64_t)blk * a.sb + (int64_t)t * a.st + (int64_t)it.h * a.sh;
@@ -630,17 +758,27 @@ struct SimtPath {
         }
       }
     }
+    __syncthreads();
 #pragma unroll
     for (int g = 0; g < GM; ++g) {
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) wb_o[(w * GM + g) * D + lane + 32 * i] = o[g][i];
+      for (int i = 0; i < kPer; ++i) wb_o[(w * GM + g) * wb_stride<D>() + lane + 32 * i] = o[g][i];
       if (lane == 0) {
         wb_ml[(w * GM + g) * 2] = m_run[g];
         wb_ml[(w * GM + g) * 2 + 1] = l_run[g];
       }
     }
+    return true;
   }
 };
+
+template <class Path, int D>
+constexpr size_t kernel_smem_bytes() {
+  // 1 KB alignment slack + ring/warp states + item partial (16 rows) +
+  // barriers + page list, count and flags
+  return 1024 + Path::ring_bytes() + (size_t)Path::kGP * D * 4 + Path::kGP * 2 * 4 + kNW * kStages * 8 +
+         (2 * kMaxItemPages + 4) * 4;
+}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -652,55 +790,64 @@ attend_kernel(const __grid_constant__ AttendArgs a) {
   const uint32_t base_u32 = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024 - (base_u32 & 1023)) & 1023);
 
-  constexpr size_t kRing = Path::smem_bytes() - 1024 - (size_t)16 * D * 4 - 16 * 2 * 4 -
-                           kNW * kStages * 8 - (kMaxItemPages + 4) * 4;
+  constexpr size_t kRing = Path::ring_bytes();
   uint8_t* ring = smem;
   float* wb_o = reinterpret_cast<float*>(smem);
-  float* wb_ml = wb_o + (size_t)kNW * Path::kGP * D;
+  float* wb_ml = wb_o + (size_t)kNW * Path::kGP * wb_stride<D>();
   float* ip_o = reinterpret_cast<float*>(smem + kRing);
-  float* ip_ml = ip_o + 16 * D;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ip_ml + 16 * 2);
+  float* ip_ml = ip_o + Path::kGP * D;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ip_ml + Path::kGP * 2);
   int* list = reinterpret_cast<int*>(bars + kNW * kStages);
-  int* cnt = list + kMaxItemPages;
+  int* blist = list + kMaxItemPages;
+  int* cnt = blist + kMaxItemPages;
   int* flag_last = cnt + 1;
-
-  pdl_wait();
-
-  const ItemInfo it = item_info(a);
-  if (!it.active) return;
+  int* flag_fail = cnt + 2;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNW * kStages; ++i) mbar_init(&bars[i], 1);
     fence_mbar_init();
+    *flag_fail = 0;
   }
-  build_page_list(a, it, list, cnt);
+  pdl_wait();
+  const int n_total = n_total_items(a);
   __syncthreads();
-  const int n = *cnt;
+  uint32_t gpage = 0;  // pages this warp has streamed through its ring so far
 
-  Path::run(a, it, ring, bars, list, n, wb_o, wb_ml);
-  __syncthreads();
-  merge_warps<D>(a.G, Path::kGP, wb_o, wb_ml, ip_o, ip_ml);
-  __syncthreads();
-
-  if (it.expected == 1) {
-    finalize_head<D>(a, it, ip_o, ip_ml, true);
-    return;
-  }
-  // publish this item's partial, then take a ticket for (b, h)
-  const int64_t item = blockIdx.x;
-  for (int e = threadIdx.x; e < a.G * D; e += kNW * 32) a.part_o[item * a.G * D + e] = ip_o[e];
-  for (int e = threadIdx.x; e < a.G * 2; e += kNW * 32) a.part_ml[item * a.G * 2 + e] = ip_ml[e];
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int prev = atomicAdd(&a.head_done[it.bh], 1);
-    *flag_last = (prev == it.expected - 1) ? 1 : 0;
-  }
-  __syncthreads();
-  if (*flag_last) {
-    __threadfence();
-    finalize_head<D>(a, it, ip_o, ip_ml, false);
-    if (threadIdx.x == 0) a.head_done[it.bh] = 0;
+  for (int v = blockIdx.x; v < n_total; v += gridDim.x) {
+    const ItemInfo it = decode_item(a, v);
+    if (!it.active) continue;
+    build_page_list(a, it, list, blist, cnt);
+    __syncthreads();
+    const int n = *cnt;
+    if (!Path::run(a, it, ring, bars, list, blist, n, wb_o, wb_ml, gpage)) *flag_fail = 1;
+    __syncthreads();
+    if (*flag_fail) return;  // a copy never arrived: stop without touching outputs
+    merge_warps<D>(a.G, Path::kGP, wb_o, wb_ml, ip_o, ip_ml);
+    __syncthreads();
+    if (it.expected == 1) {
+      finalize_head<D>(a, it, ip_o, ip_ml, true, nullptr, 0);
+    } else {
+      // publish this item's partial, then take a ticket for (b, h)
+      const int64_t slot = it.slot;
+      for (int e = threadIdx.x; e < a.G * D; e += kNW * 32)
+        a.part_o[slot * a.G * D + e] = ip_o[e];
+      for (int e = threadIdx.x; e < a.G * 2; e += kNW * 32)
+        a.part_ml[slot * a.G * 2 + e] = ip_ml[e];
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&a.head_done[it.bh], 1);
+        *flag_last = (prev == it.expected - 1) ? 1 : 0;
+      }
+      __syncthreads();
+      if (*flag_last) {
+        __threadfence();
+        finalize_head<D>(a, it, ip_o, ip_ml, false, reinterpret_cast<float*>(ring),
+                         (int)(kRing / 4));
+        if (threadIdx.x == 0) a.head_done[it.bh] = 0;
+      }
+    }
+    __syncthreads();  // shared buffers are rewritten by the next item
   }
 }
 
@@ -778,26 +925,22 @@ bool cached_pool_map(CUtensorMap* out, const void* base, const KvView& kv) {
 ItemCfg item_cfg(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense) {
   ItemCfg c;
   const int heads = q.B * kv.hkv;
-  const int target = 8 * num_sms();  // aim for several waves of resident CTAs
+  // aim for about two items per resident CTA slot (2 CTAs per SM)
+  const int target = 4 * num_sms();
   if (dense) {
-    c.cd = 8;
+    c.cd = kMaxItemPages;
     c.nd = 0;
   } else {
-    int per_head = (target + heads - 1) / heads;
-    int cd = (max_sel + per_head - 1) / max(per_head, 1);
+    const int per_head = (target + heads - 1) / heads;
+    int cd = (max_sel + per_head - 1) / per_head;
     cd = ((cd + kNW - 1) / kNW) * kNW;
     c.cd = cd < 8 ? 8 : (cd > kMaxItemPages ? kMaxItemPages : cd);
     c.nd = (max_sel + c.cd - 1) / c.cd;
     if (c.nd < 1) c.nd = 1;
   }
-  if (recover || dense) {
-    c.cc = kMaxItemPages;
-    c.nc = (q.W + c.cc - 1) / c.cc;
-    if (c.nc < 1) c.nc = 1;
-  } else {
-    c.cc = kMaxItemPages;
-    c.nc = 0;
-  }
+  c.cc = kMaxItemPages;
+  c.nc = (recover || dense) ? (q.W + c.cc - 1) / c.cc : 0;
+  if ((recover || dense) && c.nc < 1) c.nc = 1;
   c.iph = c.nd + c.nc;
   return c;
 }
@@ -810,50 +953,60 @@ bool use_mma(const QView& q, const KvView& kv) {
 }
 
 template <class Path, int D>
-cudaError_t launch_path(const AttendArgs& a, int grid, cudaStream_t s, bool pdl) {
-  constexpr size_t smem = Path::smem_bytes();
-  static bool attr_set[64] = {};
+cudaError_t launch_path(const AttendArgs& a, int max_items, cudaStream_t s, bool pdl) {
+  constexpr size_t smem = kernel_smem_bytes<Path, D>();
+  // resident CTAs per SM, measured once per device (the attribute is per device)
+  static int ctas_per_sm[64] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attend_kernel<Path, D>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!ctas_per_sm[dev]) {
+    e = cudaFuncSetAttribute(attend_kernel<Path, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem);
     if (e != cudaSuccess) return e;
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    int occ = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, attend_kernel<Path, D>, kNW * 32,
+                                                      smem);
+    if (e != cudaSuccess) return e;
+    ctas_per_sm[dev] = occ < 1 ? 1 : occ;
   }
+  int grid = num_sms() * ctas_per_sm[dev];
+  if (grid > max_items) grid = max_items;
+  if (grid < 1) grid = 1;
   return launch_k(attend_kernel<Path, D>, dim3(grid), dim3(kNW * 32), smem, s, pdl, a);
 }
 
 template <typename T, int D>
-cudaError_t dispatch_mma(const AttendArgs& a, int grid, cudaStream_t s, bool pdl) {
-  if (a.G <= 8) return launch_path<MmaPath<T, D, 1>, D>(a, grid, s, pdl);
-  return launch_path<MmaPath<T, D, 2>, D>(a, grid, s, pdl);
+cudaError_t dispatch_mma(const AttendArgs& a, int max_items, cudaStream_t s, bool pdl) {
+  if (a.G <= 8) return launch_path<MmaPath<T, D, 1>, D>(a, max_items, s, pdl);
+  return launch_path<MmaPath<T, D, 2>, D>(a, max_items, s, pdl);
 }
 
 template <typename T, typename TQ, int D>
-cudaError_t dispatch_simt_g(const AttendArgs& a, int grid, cudaStream_t s, bool pdl) {
-  if (a.G <= 4) return launch_path<SimtPath<T, TQ, D, 4>, D>(a, grid, s, pdl);
-  if (a.G <= 8) return launch_path<SimtPath<T, TQ, D, 8>, D>(a, grid, s, pdl);
-  return launch_path<SimtPath<T, TQ, D, 16>, D>(a, grid, s, pdl);
+cudaError_t dispatch_simt_g(const AttendArgs& a, int max_items, cudaStream_t s, bool pdl) {
+  if (a.G <= 4) return launch_path<SimtPath<T, TQ, D, 4>, D>(a, max_items, s, pdl);
+  if (a.G <= 8) return launch_path<SimtPath<T, TQ, D, 8>, D>(a, max_items, s, pdl);
+  return launch_path<SimtPath<T, TQ, D, 16>, D>(a, max_items, s, pdl);
 }
 
 template <typename T, typename TQ>
-cudaError_t dispatch_simt_d(const AttendArgs& a, int d, int grid, cudaStream_t s, bool pdl) {
+cudaError_t dispatch_simt_d(const AttendArgs& a, int d, int max_items, cudaStream_t s, bool pdl) {
   switch (d) {
-    case 64: return dispatch_simt_g<T, TQ, 64>(a, grid, s, pdl);
-    case 128: return dispatch_simt_g<T, TQ, 128>(a, grid, s, pdl);
-    case 256: return dispatch_simt_g<T, TQ, 256>(a, grid, s, pdl);
+    case 64: return dispatch_simt_g<T, TQ, 64>(a, max_items, s, pdl);
+    case 128: return dispatch_simt_g<T, TQ, 128>(a, max_items, s, pdl);
+    case 256: return dispatch_simt_g<T, TQ, 256>(a, max_items, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename T>
-cudaError_t dispatch_simt_q(const AttendArgs& a, int qdt, int d, int grid, cudaStream_t s,
+cudaError_t dispatch_simt_q(const AttendArgs& a, int qdt, int d, int max_items, cudaStream_t s,
                             bool pdl) {
   switch (qdt) {
-    case CVSA_DTYPE_BF16: return dispatch_simt_d<T, __nv_bfloat16>(a, d, grid, s, pdl);
-    case CVSA_DTYPE_F16: return dispatch_simt_d<T, __half>(a, d, grid, s, pdl);
-    case CVSA_DTYPE_F32: return dispatch_simt_d<T, float>(a, d, grid, s, pdl);
+    case CVSA_DTYPE_BF16: return dispatch_simt_d<T, __nv_bfloat16>(a, d, max_items, s, pdl);
+    case CVSA_DTYPE_F16: return dispatch_simt_d<T, __half>(a, d, max_items, s, pdl);
+    case CVSA_DTYPE_F32: return dispatch_simt_d<T, float>(a, d, max_items, s, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -867,14 +1020,16 @@ bool attend_supported(const QView& q, const KvView& kv) {
   return true;
 }
 
+int attend_complement_chunk() { return kMaxItemPages; }
+
 size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, bool recover,
                               bool dense) {
   const ItemCfg ic = item_cfg(q, kv, max_sel, recover, dense);
-  const size_t grid = (size_t)q.B * kv.hkv * ic.iph;
+  const size_t slots = (size_t)q.B * kv.hkv * ic.iph;
   const int G = q.hq / kv.hkv;
   size_t bytes = 0;
-  bytes += grid * G * kv.d * 4;            // part_o
-  bytes += grid * G * 2 * 4;               // part_ml
+  bytes += slots * G * kv.d * 4;            // part_o
+  bytes += slots * G * 2 * 4;               // part_ml
   bytes = (bytes + 255) & ~size_t(255);
   return bytes;
 }
@@ -914,6 +1069,7 @@ cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& 
   a.accept = p.accept;
   a.bitmap = p.bitmap;
   a.bitmap_words = p.bitmap_words;
+  a.comp_off = p.comp_off;
   a.external_draft = p.external_draft ? 1 : 0;
   a.ext_o = p.ext_o;
   a.ext_m = p.ext_m;
@@ -943,37 +1099,40 @@ cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& 
     if (a.ic.nc < 1) a.ic.nc = 1;
     a.ic.iph = a.ic.nc;
   }
-  const size_t grid = (size_t)q.B * kv.hkv * a.ic.iph;
+  a.heads = q.B * kv.hkv;
+  const size_t slots = (size_t)a.heads * a.ic.iph;
   const int G = a.G;
   a.part_o = reinterpret_cast<float*>(p.partials);
-  a.part_ml = a.part_o + grid * G * kv.d;
+  a.part_ml = a.part_o + slots * G * kv.d;
   a.head_done = p.head_done;
   a.scale = 1.0f / sqrtf((float)kv.d);
-  if (grid == 0) return cudaSuccess;
-  if (grid > 0x7fffffff) return cudaErrorInvalidValue;
-  if ((size_t)q.B * kv.hkv > (size_t)kMaxHeadsPerCall) return cudaErrorInvalidValue;
-  if (p.partial_bytes < grid * G * (kv.d + 2) * 4) return cudaErrorInvalidValue;
+  if (slots == 0) return cudaSuccess;
+  if (slots > 0x7fffffff) return cudaErrorInvalidValue;
+  if ((size_t)a.heads > (size_t)kMaxHeadsPerCall) return cudaErrorInvalidValue;
+  if (p.partial_bytes < slots * G * (kv.d + 2) * 4) return cudaErrorInvalidValue;
+  // upper bound of the virtual item space (the grid never exceeds it)
+  const int max_items = (int)slots;
 
   if (mma) {
     if (kv.dtype == CVSA_DTYPE_BF16) {
       switch (kv.d) {
-        case 64: return dispatch_mma<__nv_bfloat16, 64>(a, (int)grid, s, pdl);
-        case 128: return dispatch_mma<__nv_bfloat16, 128>(a, (int)grid, s, pdl);
-        case 256: return dispatch_mma<__nv_bfloat16, 256>(a, (int)grid, s, pdl);
+        case 64: return dispatch_mma<__nv_bfloat16, 64>(a, max_items, s, pdl);
+        case 128: return dispatch_mma<__nv_bfloat16, 128>(a, max_items, s, pdl);
+        case 256: return dispatch_mma<__nv_bfloat16, 256>(a, max_items, s, pdl);
       }
     } else {
       switch (kv.d) {
-        case 64: return dispatch_mma<__half, 64>(a, (int)grid, s, pdl);
-        case 128: return dispatch_mma<__half, 128>(a, (int)grid, s, pdl);
-        case 256: return dispatch_mma<__half, 256>(a, (int)grid, s, pdl);
+        case 64: return dispatch_mma<__half, 64>(a, max_items, s, pdl);
+        case 128: return dispatch_mma<__half, 128>(a, max_items, s, pdl);
+        case 256: return dispatch_mma<__half, 256>(a, max_items, s, pdl);
       }
     }
     return cudaErrorInvalidValue;
   }
   switch (kv.dtype) {
-    case CVSA_DTYPE_F32: return dispatch_simt_q<float>(a, q.dtype, kv.d, (int)grid, s, pdl);
-    case CVSA_DTYPE_BF16: return dispatch_simt_q<__nv_bfloat16>(a, q.dtype, kv.d, (int)grid, s, pdl);
-    case CVSA_DTYPE_F16: return dispatch_simt_q<__half>(a, q.dtype, kv.d, (int)grid, s, pdl);
+    case CVSA_DTYPE_F32: return dispatch_simt_q<float>(a, q.dtype, kv.d, max_items, s, pdl);
+    case CVSA_DTYPE_BF16: return dispatch_simt_q<__nv_bfloat16>(a, q.dtype, kv.d, max_items, s, pdl);
+    case CVSA_DTYPE_F16: return dispatch_simt_q<__half>(a, q.dtype, kv.d, max_items, s, pdl);
   }
   return cudaErrorInvalidValue;
 }

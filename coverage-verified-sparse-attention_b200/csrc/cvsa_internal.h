@@ -81,6 +81,13 @@ struct SelectParams {
   int has_cache;
   int lazy_stats;
   int32_t* step_flags;        // [1] or null
+  // compact list of the attention kernel's complement items (recovery): per
+  // head ceil(n_valid / comp_chunk) items when its new gate rejects and the
+  // batch rescored, else 0; the last CTA writes the exclusive scan.
+  int32_t* comp_cnt;          // [B*Hkv] or null
+  int32_t* comp_off;          // [B*Hkv + 1]
+  int comp_chunk;
+  int recover;                // the attention kernel recovers rejected heads (page counts)
 };
 cudaError_t launch_select_gate(const SelectParams& p, cudaStream_t s, bool pdl);
 
@@ -112,6 +119,8 @@ struct AttendParams {
   const uint8_t* accept;          // [B, Hkv]
   const uint32_t* bitmap;         // [B, Hkv, bitmap_words]
   int bitmap_words;
+  const int32_t* comp_off;        // [heads + 1] complement-item offsets (select kernel), or
+                                  // null: every head's complement chunks are enumerated
   bool external_draft;            // recover_merge: draft partial given, not recomputed
   const float* ext_o; const float* ext_m; const float* ext_l;
   // copy the source-1 selection into source 0 when source 1 was used
@@ -120,7 +129,7 @@ struct AttendParams {
   // outputs
   void* out; int out_dtype;       // normalised output or null
   float* o_unnorm; float* m_out; float* l_out;  // draft partial or null
-  int64_t* counters;              // pages attended, or null
+  int64_t* counters;              // pages attended / max, or null (CTA 0 reduces them)
   int32_t* dev_err;
   // gate outputs of the selection actually decoded (nullable): source 0's
   // gate (acc0/cov0, nullable = accepted) or source 1's (acc1/cov1)
@@ -138,6 +147,7 @@ size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, boo
 cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& p,
                           int max_sel, cudaStream_t s, bool pdl);
 bool attend_supported(const QView& q, const KvView& kv);
+int attend_complement_chunk();  // logical pages per complement item
 
 // ---- merge.cu ----
 cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,

@@ -127,12 +127,14 @@ score_pages_kernel(const TQ* __restrict__ q, const T* __restrict__ kc,
       for (int i = 0; i < VN; ++i) qf[i] = Elem<TQ>::to_f(Elem<TQ>::from_f(acc[i] * inv));
     }
 
+    // the unit's block-table entries, one per lane, fetched together up front
+    const int my_blk = (p0 + lane < min(p1, nv)) ? tables[(int64_t)b * W + p0 + lane] : -1;
     for (int p = p0; p < p1; ++p) {
+      const int blk = __shfl_sync(0xffffffffu, my_blk, p - p0);
       if (p >= nv) {
         if (head_ok && sub == 0) srow[p] = neg_inf();
         continue;
       }
-      int blk = tables[(int64_t)b * W + p];
       const bool blk_ok = blk >= 0 && blk < num_blocks;
       if (!blk_ok) {
         if (lane == 0) set_dev_error(dev_err, CVSA_DEV_ERR_BLOCK_RANGE);

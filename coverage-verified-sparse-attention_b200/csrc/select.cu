@@ -1,4 +1,4 @@
-// Top-k page selection + coverage gate, one CTA per (sequence b, kv head h).
+// Top-k page selection + coverage gate per (sequence b, kv head h).
 //
 // Restates, for one (b, h) row of page scores:
 //   * cvsa/backend.py:690,737-747 -- the top `budget` pages by score, with
@@ -7,15 +7,23 @@
 //     (both off by default);
 //   * cvsa/kernels/coverage.py:160-215 -- cov = exp(lse(scores[sel]) -
 //     lse(scores[all W pages])), max seeded with -1e20, log(sum + 1e-30),
-//     accept = cov >= tau;
+//     accept = cov >= tau; the selected scores are summed over the list
+//     entries, as the reference gathers them;
 //   * cvsa/backend.py:424-446 -- in lazy mode, the same gate on the CACHED
 //     selection, reduced over the whole batch on the device (the reference's
 //     host-side accept_mask.all()) by the last CTA to finish.
-// Top-k is an exact radix select on order-preserving 32-bit keys (4 passes
-// of 8 bits, warp-aggregated shared-memory histograms), then ties at the
-// threshold key go to the lowest page indices via a block prefix scan. The
-// selection is emitted in ascending page order together with a bitmap of it
-// (consumed by the fused recovery kernel to skip selected pages).
+// The k-th largest score is found exactly on order-preserving 32-bit keys;
+// ties at that key go to the lowest page indices through a prefix count, and
+// the selection is written in ascending page order with a bitmap of it (read
+// by the fused recovery kernel to skip selected pages). Two variants:
+//   * tables of up to 1024 pages: one WARP per (b, h), scores in registers
+//     (lane l owns a contiguous run of pages), the threshold by a 32-step
+//     bisection on the key (one warp reduction per step), no block barriers;
+//   * longer tables: one CTA per (b, h), scores in shared memory, a 4-pass
+//     8-bit radix select with warp-aggregated shared histograms.
+// Both finish with the batch-global decision and, for the attention kernel,
+// the exclusive scan of each head's complement-item count (rejected heads
+// only), taken by the last CTA to finish: no host synchronisation.
 #include "cvsa_common.cuh"
 #include "cvsa_internal.h"
 #include "cvsa_launch.cuh"
@@ -54,6 +62,18 @@ struct BlockScan {
     return excl;
   }
 };
+
+__device__ __forceinline__ int warp_excl_scan(int v, int& total) {
+  const int lane = threadIdx.x & 31;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  total = __shfl_sync(0xffffffffu, x, 31);
+  return x - v;
+}
 
 template <int NT>
 __device__ float block_reduce_max(float v, float* red) {
@@ -105,6 +125,270 @@ __device__ float lse_flagged(const float* s, const uint8_t* flag, int W, float* 
   return m + logf(sum + 1e-30f);
 }
 
+// log-sum-exp over the entries of an index list (duplicates count, like the
+// reference's gather at coverage.py:196-204); warp-cooperative.
+__device__ __forceinline__ float lse_list_warp(const float* row, int W, const int32_t* idx,
+                                               int n) {
+  const int lane = threadIdx.x & 31;
+  float m = -1e20f;
+  for (int i = lane; i < n; i += 32) {
+    const int pg = idx[i];
+    if (pg >= 0 && pg < W) m = fmaxf(m, row[pg]);
+  }
+  m = fmaxf(warp_max(m), -1e20f);
+  float sum = 0.f;
+  for (int i = lane; i < n; i += 32) {
+    const int pg = idx[i];
+    if (pg >= 0 && pg < W) sum += expf(row[pg] - m);
+  }
+  sum = warp_sum(sum);
+  return m + logf(sum + 1e-30f);
+}
+
+__device__ __forceinline__ void count_head(const SelectParams& p, bool acc) {
+  if (!p.counters) return;
+  atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_ACCEPT]),
+            (unsigned long long)(acc ? 1 : 0));
+  atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_TOTAL]), 1ull);
+}
+
+// Last-CTA epilogue shared by both variants: batch-global decision, step
+// statistics, flags, and the exclusive scan of the complement-item counts.
+// Every thread of every CTA calls it; `cta_rejects` is read in thread 0.
+template <int NT>
+__device__ void finish_select(const SelectParams& p, int cta_rejects, int* s_flag, int* wsum) {
+  if (!p.sync_ctr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (cta_rejects) atomicAdd(&p.sync_ctr[1], cta_rejects);
+    __threadfence();
+    const int done = atomicAdd(&p.sync_ctr[0], 1);
+    s_flag[0] = (done == (int)gridDim.x - 1) ? 1 : 0;
+  }
+  __syncthreads();
+  if (!s_flag[0]) return;
+  __threadfence();
+  if (threadIdx.x == 0) {
+    const int rejects = atomicAdd(&p.sync_ctr[1], 0);
+    int all_accept;
+    if (p.mode == CVSA_MODE_LAZY) {
+      all_accept = (p.has_cache && rejects == 0) ? 1 : 0;
+    } else {
+      all_accept = (rejects == 0) ? 1 : 0;
+    }
+    if (p.decision) p.decision[0] = all_accept;
+    if (p.counters) {
+      unsigned long long* c = reinterpret_cast<unsigned long long*>(p.counters);
+      if (p.mode == CVSA_MODE_LAZY) {
+        atomicAdd(&c[CVSA_CTR_COVERAGE_CHECKS], 1ull);
+        if (all_accept) {
+          atomicAdd(&c[CVSA_CTR_ACCEPT_STEPS], 1ull);
+        } else {
+          atomicAdd(&c[CVSA_CTR_REJECT_STEPS], 1ull);
+          atomicAdd(&c[CVSA_CTR_SCORING_STEPS], 1ull);
+        }
+      } else {
+        atomicAdd(&c[CVSA_CTR_SCORING_STEPS], 1ull);
+        if (!p.lazy_stats)
+          atomicAdd(&c[all_accept ? CVSA_CTR_ACCEPT_STEPS : CVSA_CTR_REJECT_STEPS], 1ull);
+      }
+    }
+    if (p.step_flags) {
+      int fl = 0;
+      if (p.mode == CVSA_MODE_LAZY) fl = all_accept ? 1 : 2;
+      else fl = (all_accept ? 1 : 0) | 2;
+      p.step_flags[0] = fl;
+    }
+    s_flag[1] = all_accept;
+  }
+  __syncthreads();
+  if (p.comp_off) {
+    const int heads = p.B * p.hkv;
+    const bool reuse = (p.mode == CVSA_MODE_LAZY) && s_flag[1];
+    int carry = 0;
+    for (int base = 0; base < heads; base += NT) {
+      const int i = base + threadIdx.x;
+      const int v = (i < heads && !reuse) ? __ldcg(&p.comp_cnt[i]) : 0;
+      int tot = 0;
+      const int ex = BlockScan<NT>::exclusive(v, wsum, tot);
+      if (i < heads) p.comp_off[i] = carry + ex;
+      carry += tot;
+    }
+    if (threadIdx.x == 0) p.comp_off[heads] = carry;
+  }
+  if (threadIdx.x == 0) {
+    p.sync_ctr[1] = 0;
+    __threadfence();
+    p.sync_ctr[0] = 0;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// warp per (b, h): tables of up to 32 * EPL pages
+// ---------------------------------------------------------------------------
+constexpr int kWarpSelWarps = 8;
+
+template <int EPL>
+__global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(SelectParams p) {
+  constexpr int NT = kWarpSelWarps * 32;
+  __shared__ int wsum[NT / 32];
+  __shared__ int s_flag[2];
+  __shared__ int s_rej;
+  if (threadIdx.x == 0) s_rej = 0;
+  __syncthreads();
+  pdl_wait();
+
+  const int lane = threadIdx.x & 31;
+  const int heads = p.B * p.hkv;
+  const int bh = blockIdx.x * kWarpSelWarps + (threadIdx.x >> 5);
+  if (bh < heads) {
+    const int b = bh / p.hkv;
+    const int W = p.W;
+    const int nv = min(n_valid_pages(p.lens[b], p.bs), W);
+    const float* row = p.scores + (int64_t)bh * W;
+    const int p0 = lane * EPL;
+    float s[EPL];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) s[i] = (p0 + i < W) ? __ldg(row + p0 + i) : neg_inf();
+
+    // lse over all W pages (coverage.py:179-195): -inf entries contribute 0
+    float m = -1e20f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) m = fmaxf(m, s[i]);
+    m = fmaxf(warp_max(m), -1e20f);
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) sum += expf(s[i] - m);
+    const float lse_all = m + logf(warp_sum(sum) + 1e-30f);
+
+    // ---- cached-selection gate (lazy) ----
+    if (p.mode == CVSA_MODE_LAZY && p.has_cache && p.cached_idx) {
+      const int nc = min(max(p.cached_n[bh], 0), p.cached_stride);
+      const float lse_c =
+          lse_list_warp(row, W, p.cached_idx + (int64_t)bh * p.cached_stride, nc);
+      const float cov = expf(lse_c - lse_all);
+      const bool acc = cov >= p.tau;
+      if (lane == 0) {
+        if (p.cached_accept) p.cached_accept[bh] = acc ? 1 : 0;
+        if (p.cached_cov) p.cached_cov[bh] = cov;
+        if (!acc) atomicAdd(&s_rej, 1);
+        count_head(p, acc);
+      }
+    }
+
+    // ---- new selection ----
+    if (p.sel_idx) {
+      const int sink = p.sink, local = p.local;
+      bool cand[EPL], forced[EPL];
+      int nf = 0;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const int pg = p0 + i;
+        forced[i] = pg < nv && (pg < sink || pg >= nv - local);
+        cand[i] = pg < nv && !forced[i];
+        nf += forced[i] ? 1 : 0;
+      }
+      const int n_cand = nv - (int)__reduce_add_sync(0xffffffffu, (unsigned)nf);
+      const int k = min(p.budget, n_cand);
+      const bool all_cand = k >= n_cand;
+      uint32_t key[EPL];
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) key[i] = float_key(s[i]);
+      uint32_t thr = 0;
+      int take_eq = 0;
+      if (k > 0 && !all_cand) {
+        // largest T with #{candidates with key >= T} >= k, bit by bit
+#pragma unroll 1
+        for (int bit = 31; bit >= 0; --bit) {
+          const uint32_t c = thr | (1u << bit);
+          unsigned cnt = 0;
+#pragma unroll
+          for (int i = 0; i < EPL; ++i) cnt += (cand[i] && key[i] >= c) ? 1u : 0u;
+          if ((int)__reduce_add_sync(0xffffffffu, cnt) >= k) thr = c;
+        }
+        unsigned gt = 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) gt += (cand[i] && key[i] > thr) ? 1u : 0u;
+        take_eq = k - (int)__reduce_add_sync(0xffffffffu, gt);
+      }
+      int my_eq = 0;
+      if (k > 0 && !all_cand) {
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) my_eq += (cand[i] && key[i] == thr) ? 1 : 0;
+      }
+      int tot_eq = 0;
+      int rank = warp_excl_scan(my_eq, tot_eq);
+      bool sel[EPL];
+      int my_sel = 0;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        bool t = forced[i];
+        if (cand[i] && k > 0) {
+          if (all_cand) {
+            t = true;
+          } else if (key[i] > thr) {
+            t = true;
+          } else if (key[i] == thr) {
+            t = rank < take_eq;
+            ++rank;
+          }
+        }
+        sel[i] = t;
+        my_sel += t ? 1 : 0;
+      }
+      int n_sel = 0;
+      int pos = warp_excl_scan(my_sel, n_sel);
+      int32_t* out = p.sel_idx + (int64_t)bh * p.max_sel;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (sel[i]) {
+          if (pos < p.max_sel) out[pos] = p0 + i;
+          ++pos;
+        }
+      if (p.sel_bitmap) {
+        constexpr int LPW = (EPL >= 32) ? 1 : 32 / EPL;  // lanes per 32-bit word
+        uint32_t bits = 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) bits |= sel[i] ? (1u << i) : 0u;
+        uint32_t word = (EPL >= 32) ? bits : (bits << ((lane % LPW) * EPL));
+#pragma unroll
+        for (int o = LPW / 2; o >= 1; o >>= 1) word |= __shfl_xor_sync(0xffffffffu, word, o);
+        const int wi = lane / LPW;
+        if (lane % LPW == 0 && wi < p.bitmap_words)
+          p.sel_bitmap[(int64_t)bh * p.bitmap_words + wi] = word;
+      }
+      // coverage of the new selection
+      float ms = -1e20f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (sel[i]) ms = fmaxf(ms, s[i]);
+      ms = fmaxf(warp_max(ms), -1e20f);
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < EPL; ++i)
+        if (sel[i]) ss += expf(s[i] - ms);
+      const float lse_s = ms + logf(warp_sum(ss) + 1e-30f);
+      const float cov = expf(lse_s - lse_all);
+      const bool acc = cov >= p.tau;
+      if (lane == 0) {
+        p.sel_n[bh] = min(n_sel, p.max_sel);
+        if (p.accept) p.accept[bh] = acc ? 1 : 0;
+        if (p.cov) p.cov[bh] = cov;
+        if (p.comp_cnt) p.comp_cnt[bh] = acc ? 0 : (nv + p.comp_chunk - 1) / p.comp_chunk;
+        if (p.mode == CVSA_MODE_SCORE) {
+          if (!acc) atomicAdd(&s_rej, 1);
+          if (!p.lazy_stats) count_head(p, acc);
+        }
+      }
+    }
+  }
+  finish_select<NT>(p, s_rej, s_flag, wsum);
+  pdl_launch_dependents();
+}
+
+// ---------------------------------------------------------------------------
+// CTA per (b, h): long tables
+// ---------------------------------------------------------------------------
 template <int NT>
 __global__ void __launch_bounds__(NT) select_gate_kernel(SelectParams p) {
   extern __shared__ float s_scores[];  // [W] then uint8 flags [W]
@@ -112,6 +396,7 @@ __global__ void __launch_bounds__(NT) select_gate_kernel(SelectParams p) {
   __shared__ int wsum[NT / 32];
   __shared__ uint32_t hist[256];
   __shared__ int bcast[4];
+  __shared__ int s_flag[2];
 
   pdl_wait();
 
@@ -136,31 +421,21 @@ __global__ void __launch_bounds__(NT) select_gate_kernel(SelectParams p) {
   const float lse_all = m_all + logf(block_reduce_sum<NT>(sum, red) + 1e-30f);
 
   const float tau = p.tau;
-  bool deciding_reject = false;
+  int rejects = 0;  // of the deciding gate, thread 0
 
   // ---- cached-selection gate (lazy) ----
-  const bool do_cached = (p.mode == CVSA_MODE_LAZY) && p.has_cache && p.cached_idx;
-  if (do_cached) {
-    for (int i = tid; i < W; i += NT) flag[i] = 0;
-    __syncthreads();
-    const int nc = p.cached_n[bh];
-    const int32_t* ci = p.cached_idx + (int64_t)bh * p.cached_stride;
-    for (int i = tid; i < nc; i += NT) {
-      const int pg = ci[i];
-      if (pg >= 0 && pg < W) flag[pg] = 1;
-    }
-    __syncthreads();
-    const float lse_c = lse_flagged<NT>(s_scores, flag, W, red);
-    const float cov = expf(lse_c - lse_all);
-    const bool acc = cov >= tau;
-    if (tid == 0) {
-      if (p.cached_accept) p.cached_accept[bh] = acc ? 1 : 0;
-      if (p.cached_cov) p.cached_cov[bh] = cov;
-      deciding_reject = !acc;
-      if (p.counters) {
-        atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_ACCEPT]),
-                  (unsigned long long)(acc ? 1 : 0));
-        atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_TOTAL]), 1ull);
+  if ((p.mode == CVSA_MODE_LAZY) && p.has_cache && p.cached_idx) {
+    if (tid < 32) {
+      const int nc = min(max(p.cached_n[bh], 0), p.cached_stride);
+      const float lse_c = lse_list_warp(s_scores, W, p.cached_idx + (int64_t)bh * p.cached_stride,
+                                        nc);
+      const float cov = expf(lse_c - lse_all);
+      const bool acc = cov >= tau;
+      if (tid == 0) {
+        if (p.cached_accept) p.cached_accept[bh] = acc ? 1 : 0;
+        if (p.cached_cov) p.cached_cov[bh] = cov;
+        rejects = acc ? 0 : 1;
+        count_head(p, acc);
       }
     }
     __syncthreads();
@@ -308,60 +583,14 @@ __global__ void __launch_bounds__(NT) select_gate_kernel(SelectParams p) {
       p.sel_n[bh] = min(n_sel, p.max_sel);
       if (p.accept) p.accept[bh] = acc ? 1 : 0;
       if (p.cov) p.cov[bh] = cov;
+      if (p.comp_cnt) p.comp_cnt[bh] = acc ? 0 : (nv + p.comp_chunk - 1) / p.comp_chunk;
       if (p.mode == CVSA_MODE_SCORE) {
-        deciding_reject = !acc;
-        if (p.counters && !p.lazy_stats) {
-          atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_ACCEPT]),
-                    (unsigned long long)(acc ? 1 : 0));
-          atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_TOTAL]),
-                    1ull);
-        }
+        rejects = acc ? 0 : 1;
+        if (!p.lazy_stats) count_head(p, acc);
       }
     }
   }
-
-  // ---- batch-global decision by the last CTA (no host sync) ----
-  if (p.sync_ctr && tid == 0) {
-    if (deciding_reject) atomicAdd(&p.sync_ctr[1], 1);
-    __threadfence();
-    const int done = atomicAdd(&p.sync_ctr[0], 1);
-    if (done == (int)gridDim.x - 1) {
-      __threadfence();
-      const int rejects = atomicAdd(&p.sync_ctr[1], 0);
-      int all_accept;
-      if (p.mode == CVSA_MODE_LAZY) {
-        all_accept = (p.has_cache && rejects == 0) ? 1 : 0;
-      } else {
-        all_accept = (rejects == 0) ? 1 : 0;
-      }
-      if (p.decision) p.decision[0] = all_accept;
-      if (p.counters) {
-        unsigned long long* c = reinterpret_cast<unsigned long long*>(p.counters);
-        if (p.mode == CVSA_MODE_LAZY) {
-          atomicAdd(&c[CVSA_CTR_COVERAGE_CHECKS], 1ull);
-          if (all_accept) {
-            atomicAdd(&c[CVSA_CTR_ACCEPT_STEPS], 1ull);
-          } else {
-            atomicAdd(&c[CVSA_CTR_REJECT_STEPS], 1ull);
-            atomicAdd(&c[CVSA_CTR_SCORING_STEPS], 1ull);
-          }
-        } else {
-          atomicAdd(&c[CVSA_CTR_SCORING_STEPS], 1ull);
-          if (!p.lazy_stats) atomicAdd(&c[all_accept ? CVSA_CTR_ACCEPT_STEPS
-                                                     : CVSA_CTR_REJECT_STEPS], 1ull);
-        }
-      }
-      if (p.step_flags) {
-        int fl = 0;
-        if (p.mode == CVSA_MODE_LAZY) fl = all_accept ? 1 : 2;
-        else fl = (all_accept ? 1 : 0) | 2;
-        p.step_flags[0] = fl;
-      }
-      p.sync_ctr[1] = 0;
-      __threadfence();
-      p.sync_ctr[0] = 0;
-    }
-  }
+  finish_select<NT>(p, rejects, s_flag, wsum);
   pdl_launch_dependents();
 }
 
@@ -377,6 +606,14 @@ cudaError_t launch_sel(const SelectParams& p, cudaStream_t s, bool pdl) {
   return launch_k(select_gate_kernel<NT>, dim3(p.B * p.hkv), dim3(NT), smem, s, pdl, p);
 }
 
+template <int EPL>
+cudaError_t launch_sel_warp(const SelectParams& p, cudaStream_t s, bool pdl) {
+  const int heads = p.B * p.hkv;
+  const int grid = (heads + kWarpSelWarps - 1) / kWarpSelWarps;
+  return launch_k(select_gate_warp_kernel<EPL>, dim3(grid), dim3(kWarpSelWarps * 32), 0, s, pdl,
+                  p);
+}
+
 // ---- standalone coverage gate (coverage.py:160-215) ----
 template <int NT>
 __global__ void __launch_bounds__(NT)
@@ -384,13 +621,10 @@ coverage_kernel(const float* scores, int W, const int32_t* idx, int max_sel, con
                 float tau, uint8_t* accept, float* cov_out) {
   extern __shared__ float s_sc[];
   __shared__ float red[33];
-  uint8_t* flag = reinterpret_cast<uint8_t*>(s_sc + W);
+  __shared__ float s_lse;
   const int bh = blockIdx.x;
   const float* row = scores + (int64_t)bh * W;
-  for (int i = threadIdx.x; i < W; i += NT) {
-    s_sc[i] = row[i];
-    flag[i] = 0;
-  }
+  for (int i = threadIdx.x; i < W; i += NT) s_sc[i] = row[i];
   __syncthreads();
   float m = -1e20f;
   for (int i = threadIdx.x; i < W; i += NT) m = fmaxf(m, s_sc[i]);
@@ -398,14 +632,13 @@ coverage_kernel(const float* scores, int W, const int32_t* idx, int max_sel, con
   float sum = 0.f;
   for (int i = threadIdx.x; i < W; i += NT) sum += expf(s_sc[i] - m_all);
   const float lse_all = m_all + logf(block_reduce_sum<NT>(sum, red) + 1e-30f);
-  const int ns = n[bh];
-  for (int i = threadIdx.x; i < min(ns, max_sel); i += NT) {
-    const int pg = idx[(int64_t)bh * max_sel + i];
-    if (pg >= 0 && pg < W) flag[pg] = 1;
+  if (threadIdx.x < 32) {
+    const int ns = min(max(n[bh], 0), max_sel);
+    const float l = lse_list_warp(s_sc, W, idx + (int64_t)bh * max_sel, ns);
+    if (threadIdx.x == 0) s_lse = l;
   }
   __syncthreads();
-  const float lse_s = lse_flagged<NT>(s_sc, flag, W, red);
-  const float c = expf(lse_s - lse_all);
+  const float c = expf(s_lse - lse_all);
   if (threadIdx.x == 0) {
     accept[bh] = c >= tau ? 1 : 0;
     if (cov_out) cov_out[bh] = c;
@@ -476,7 +709,10 @@ cudaError_t launch_build_bitmap(const int32_t* idx, int max_sel, const int32_t* 
 }
 
 cudaError_t launch_select_gate(const SelectParams& p, cudaStream_t s, bool pdl) {
-  if (p.W <= 1024) return launch_sel<256>(p, s, pdl);
+  if (p.W <= 128) return launch_sel_warp<4>(p, s, pdl);
+  if (p.W <= 256) return launch_sel_warp<8>(p, s, pdl);
+  if (p.W <= 512) return launch_sel_warp<16>(p, s, pdl);
+  if (p.W <= 1024) return launch_sel_warp<32>(p, s, pdl);
   if (p.W <= 8192) return launch_sel<512>(p, s, pdl);
   return launch_sel<1024>(p, s, pdl);
 }
@@ -484,7 +720,7 @@ cudaError_t launch_select_gate(const SelectParams& p, cudaStream_t s, bool pdl) 
 cudaError_t launch_check_coverage(const float* scores, int B, int hkv, int W, const int32_t* idx,
                                   int max_sel, const int32_t* n, float tau, uint8_t* accept,
                                   float* cov, cudaStream_t s) {
-  const size_t smem = (size_t)W * 5 + 16;
+  const size_t smem = (size_t)W * 4 + 16;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(coverage_kernel<256>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -42,15 +42,17 @@ from cvsa.kernels.select import budget_for
 
 
 class _LayerState:
-    __slots__ = ("key", "cached_idx", "cached_n", "has_cache", "accept", "coverage",
-                 "flags", "scores")
+    __slots__ = ("key", "cached_idx", "cached_n", "has_cache", "accept", "accept_bool",
+                 "coverage", "flags", "scores", "ckey", "kvd", "qd", "cfg", "io", "ws_bytes")
 
     def __init__(self, key, B, Hkv, max_sel, W, device, keep_scores):
         self.key = key
+        self.ckey = None
         self.cached_idx = torch.zeros((B, Hkv, max_sel), dtype=torch.int32, device=device)
         self.cached_n = torch.zeros((B, Hkv), dtype=torch.int32, device=device)
         self.has_cache = False
         self.accept = torch.ones((B, Hkv), dtype=torch.uint8, device=device)
+        self.accept_bool = self.accept.view(torch.bool)
         self.coverage = torch.ones((B, Hkv), dtype=torch.float32, device=device)
         self.flags = torch.zeros((1,), dtype=torch.int32, device=device)
         self.scores = (torch.empty((B, Hkv, W), dtype=torch.float32, device=device)
@@ -144,6 +146,7 @@ class CVSABackend:
         self.keep_page_scores = keep_page_scores
 
         self._layers: Dict[int, _LayerState] = {}
+        self._ws: Dict[int, tuple] = {}                  # stream -> (ptr, bytes, tensor)
         self._counters: Optional[torch.Tensor] = None   # int64[8] device
         self._dev_error: Optional[torch.Tensor] = None
         self._step = 0
@@ -296,19 +299,31 @@ class CVSABackend:
         bt = bt.contiguous()
         cl = cl.contiguous()
         out = torch.empty_like(q)
-        kvd = _lib.kv_desc(k_cache, v_cache)
-        qd = _lib.query_desc(q, bt, cl)
-        cfg = _lib.StepConfig(mode, budget, self.sink_pages, self.local_pages, float(self.tau),
-                              _lib.RECOVERY_EXACT, 1 if st.has_cache else 0,
-                              1 if self.lazy else 0)
-        io = _lib.StepIO(st.cached_idx.data_ptr(), st.cached_n.data_ptr(), max_sel, 0,
-                         out.data_ptr(), _lib.ptr(st.scores), st.accept.data_ptr(),
-                         st.coverage.data_ptr(), self._counters.data_ptr(), st.flags.data_ptr(),
-                         self._dev_error.data_ptr())
         lib = _lib.load()
-        nbytes = lib.cvsa_step_workspace_size(qd, kvd, cfg, max_sel)
-        ws = _lib.WORKSPACE.get(nbytes, dev, "step")
         stream = _lib.stream_ptr(dev)
+        # descriptors are rebuilt (and validated) only when the caller's
+        # tensors change; decode loops pass the same cache and tables each step
+        ckey = (k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape, k_cache.stride(),
+                k_cache.dtype, bt.data_ptr(), cl.data_ptr(), q.shape, q.dtype, stream)
+        if st.ckey != ckey:
+            st.kvd = _lib.kv_desc(k_cache, v_cache)
+            st.qd = _lib.query_desc(q, bt, cl)
+            st.cfg = _lib.StepConfig(mode, budget, self.sink_pages, self.local_pages,
+                                     float(self.tau), _lib.RECOVERY_EXACT, 0,
+                                     1 if self.lazy else 0)
+            st.io = _lib.StepIO(st.cached_idx.data_ptr(), st.cached_n.data_ptr(), max_sel, 0,
+                                out.data_ptr(), _lib.ptr(st.scores), st.accept.data_ptr(),
+                                st.coverage.data_ptr(), self._counters.data_ptr(),
+                                st.flags.data_ptr(), self._dev_error.data_ptr())
+            st.ws_bytes = lib.cvsa_step_workspace_size(st.qd, st.kvd, st.cfg, max_sel)
+            st.ckey = ckey
+        kvd, qd, cfg, io = st.kvd, st.qd, st.cfg, st.io
+        qd.q = q.data_ptr()
+        io.out = out.data_ptr()
+        io.timing_events = None
+        cfg.mode = mode
+        cfg.has_cache = 1 if st.has_cache else 0
+        ws = self._workspace(st.ws_bytes, dev, stream)
         events = None
         if self._timing_events is not None:
             io.timing_events = ctypes.cast(self._timing_events, ctypes.c_void_p)
@@ -318,14 +333,24 @@ class CVSABackend:
                 e.record()      # torch creates the cudaEvent_t at its first record
             arr = (ctypes.c_void_p * _lib.NUM_EVENTS)(*[e.cuda_event for e in events])
             io.timing_events = ctypes.cast(arr, ctypes.c_void_p)
-        _lib.check(lib.cvsa_decode_step(qd, kvd, cfg, io, ws.data_ptr(), ws.numel(), stream),
-                   "cvsa_decode_step")
+        rc = lib.cvsa_decode_step(qd, kvd, cfg, io, ws[0], ws[1], stream)
+        if rc:
+            _lib.check(rc, "cvsa_decode_step")
         if events is not None:
             self._pending_events.append((mode, events))
         if mode in (_lib.MODE_SCORE, _lib.MODE_LAZY):
             st.has_cache = True
-            self._last_accept_mask[layer_idx] = st.accept.bool()
+            self._last_accept_mask[layer_idx] = st.accept_bool
         return out
+
+    def _workspace(self, nbytes: int, dev: torch.device, stream: int):
+        """(pointer, bytes) of a zeroed 256-aligned workspace for this stream."""
+        ws = self._ws.get(stream)
+        if ws is None or ws[1] < nbytes:
+            buf = _lib.WORKSPACE.get(nbytes, dev, f"step-{stream}")
+            ws = (buf.data_ptr(), buf.numel(), buf)
+            self._ws[stream] = ws
+        return ws
 
     # ---- tracing helpers -------------------------------------------------
     def cached_selection(self, layer_idx: int) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
