@@ -1,4 +1,6 @@
-// Sparse paged decode, fused exact recovery and LSE merge.
+// Sparse paged decode, fused exact recovery and LSE merge, for the layouts
+// the TMA stream kernel (attend_stream.cu) does not take: fp32 KV, q and KV in
+// different dtypes, or pools whose strides or base are not 16-byte aligned.
 //
 // Restates, as one split-K kernel:
 //   * the decode kernels of cvsa/kernels/sparse_decode.py (:424-500 unnorm,
@@ -15,23 +17,15 @@
 // (chunks of 32 logical pages minus the selected ones); a dense layer has
 // chunks of all valid pages. Draft items are enumerated statically; the
 // complement items of the rejected heads form a compact list whose per-head
-// offsets the selection kernel's last CTA scanned, so CTAs never wait on heads
-// that accepted. CTAs are persistent (2 per SM) and walk this item space with a
-// grid stride. A CTA of 4 warps runs one item at a time: the warps take its
-// pages round robin, each streaming them through its own 3-stage shared
-// memory ring filled by TMA (one box per 64-wide slice of head_dim for K and
-// for V, 128-byte swizzle; ring phases carry over from item to item), and each
-// keeps an online-softmax state. All G query heads of the KV head are packed
-// into the M dimension of mma.sync m16n8k16 (bf16/f16 in, f32 accumulate):
-// S = Q K^T (M = query heads, N = 16 tokens, K = head_dim, two independent
-// accumulation chains) and O += P V (K = 16 tokens, N = head_dim), with P
-// passed from the S accumulators to the A operand in registers. Warp states
-// merge in shared memory into an item partial (o, m, l) per query head. A head
-// with one item is finished by that CTA; otherwise the last CTA to finish an
-// item of the head (atomic ticket, no spin) merges the partials in a fixed
-// order -- draft chunks, then complement chunks -- so results are
-// deterministic. fp32 (and mixed-dtype) KV use a CUDA-core per-page step in the
-// same framework.
+// offsets the selection kernel's last CTA scanned. CTAs are persistent and walk
+// this item space with a grid stride. A CTA of 4 warps runs one item at a
+// time: the warps take its pages round robin and read K and V rows straight
+// from global memory (lane = head_dim columns), each keeping an online-softmax
+// state; warp states merge in shared memory into an item partial (o, m, l) per
+// query head. A head with one item is finished by that CTA; otherwise the last
+// CTA to finish an item of the head (atomic ticket, no spin) merges the
+// partials in a fixed order -- draft chunks, then complement chunks -- so
+// results are deterministic.
 #include <mutex>
 #include <unordered_map>
 
@@ -43,7 +37,7 @@ namespace cvsa {
 namespace {
 
 constexpr int kNW = 4;             // warps per CTA
-constexpr int kStages = 2;         // per-warp TMA ring depth (3 CTAs fit per SM)
+constexpr int kStages = 2;         // barrier words reserved per warp
 constexpr int kMaxItemPages = 32;  // pages per item (list capacity)
 constexpr int kBS = 16;            // tokens per page (kernels built for 16)
 
@@ -54,8 +48,6 @@ struct ItemCfg {
 };
 
 struct AttendArgs {
-  CUtensorMap kmap;  // 64-byte aligned (type alignment)
-  CUtensorMap vmap;
   const void* q;
   const void* k;
   const void* v;
@@ -443,254 +435,6 @@ __device__ void merge_warps(int G, int GP, const float* wb_o, float* wb_ml, floa
 }
 
 // ---------------------------------------------------------------------------
-// tensor-core per-page step (bf16 / f16, q dtype == kv dtype)
-// ---------------------------------------------------------------------------
-template <typename T, int D, int GR>
-struct MmaPath {
-  static constexpr int kSub = D / 64;                 // 64-wide head_dim slices
-  static constexpr int kTileBytes = kBS * 128;        // one swizzled slice
-  static constexpr int kStageBytes = 2 * kSub * kTileBytes;  // K + V
-  static constexpr int kGP = 8 * GR;                  // query rows per warp state
-  static constexpr int kNT = D / 8;                   // n-tiles of O
-
-  static constexpr size_t ring_bytes() {
-    size_t ring = (size_t)kNW * kStages * kStageBytes;
-    size_t wb = (size_t)kNW * kGP * wb_stride<D>() * 4 + (size_t)kNW * kGP * 2 * 4;
-    return ring > wb ? ring : wb;
-  }
-
-  // Returns false if a copy never arrived (the warp drained what it could).
-  __device__ static bool run(const AttendArgs& a, const ItemInfo& it, uint8_t* ring,
-                             uint64_t* bars, const int* list, const int* blist, int cnt,
-                             float* wb_o, float* wb_ml, uint32_t& gpage) {
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gq = lane >> 2, tq = lane & 3;
-    const int G = a.G;
-
-    // Q as the A operand: rows g (and g+8 for GR == 2), 16 head_dim per k-step
-    uint32_t qa[D / 16][2 * GR];
-    {
-      const T* qb = reinterpret_cast<const T*>(a.q) + ((int64_t)it.b * a.hq + (int64_t)it.h * G) * D;
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-#pragma unroll
-        for (int r = 0; r < GR; ++r) {
-          const int g = gq + 8 * r;
-          uint32_t lo = 0, hi = 0;
-          if (g < G) {
-            lo = *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * D + ks * 16 + tq * 2);
-            hi = *reinterpret_cast<const uint32_t*>(qb + (int64_t)g * D + ks * 16 + 8 + tq * 2);
-          }
-          qa[ks][r] = lo;       // a0 (row g) / a1 (row g+8)
-          qa[ks][GR + r] = hi;  // a2 / a3
-        }
-      }
-    }
-
-    float o[kNT][2 * GR];
-    float dummy[2] = {0.f, 0.f};
-#pragma unroll
-    for (int n = 0; n < kNT; ++n)
-#pragma unroll
-      for (int r = 0; r < 2 * GR; ++r) o[n][r] = 0.f;
-    float m_run[GR], l_run[GR];
-#pragma unroll
-    for (int r = 0; r < GR; ++r) {
-      m_run[r] = neg_inf();
-      l_run[r] = 0.f;
-    }
-
-    const int nmine = cnt > w ? (cnt - w + kNW - 1) / kNW : 0;
-    uint8_t* my_ring = ring + (size_t)w * kStages * kStageBytes;
-    uint64_t* my_bar = bars + w * kStages;
-
-    auto page_blk = [&](int jj) { return blist[w + jj * kNW]; };
-    auto issue = [&](int jj) {
-      if (lane == 0) {
-        const int st = (int)((gpage + jj) % kStages);
-        const int blk = page_blk(jj);
-        uint8_t* dst = my_ring + (size_t)st * kStageBytes;
-        if (blk >= 0) {
-          mbar_arrive_expect_tx(&my_bar[st], kStageBytes);
-#pragma unroll
-          for (int s = 0; s < kSub; ++s) {
-            tma_load_4d(dst + s * kTileBytes, &a.kmap, &my_bar[st], s * 64, it.h, 0, blk);
-            tma_load_4d(dst + (kSub + s) * kTileBytes, &a.vmap, &my_bar[st], s * 64, it.h, 0, blk);
-          }
-        } else {
-          mbar_arrive_expect_tx(&my_bar[st], 0);  // out-of-pool block: nothing to load
-        }
-      }
-    };
-
-    // the ring (or the warp-state buffer aliasing it) was last read before the
-    // CTA barrier that precedes this call; order those reads before the copies
-    fence_proxy_async_smem();
-    const int npro = nmine < kStages ? nmine : kStages;
-    for (int jj = 0; jj < npro; ++jj) issue(jj);
-
-    bool failed = false;
-    for (int jj = 0; jj < nmine; ++jj) {
-      const uint32_t gp = gpage + jj;
-      const int st = (int)(gp % kStages);
-      const uint32_t ph = (gp / kStages) & 1;
-      if (!mbar_wait_bounded(&my_bar[st], ph)) {
-        failed = true;
-        set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
-        // drain the copies still in flight for this warp (bounded), then stop
-        for (int k2 = jj + 1; k2 < nmine && k2 < jj + kStages; ++k2)
-          mbar_wait_bounded(&my_bar[(gpage + k2) % kStages], ((gpage + k2) / kStages) & 1);
-        break;
-      }
-      const int pg = list[w + jj * kNW];
-      const bool ok = page_blk(jj) >= 0;
-      const int ntok = ok ? min(kBS, it.ctx - pg * kBS) : 0;
-      if (ntok > 0) {
-        const uint32_t kbase = smem_u32(my_ring + (size_t)st * kStageBytes);
-        const uint32_t vbase = kbase + kSub * kTileBytes;
-        // ---- S = Q K^T over the 16 tokens, two independent k-chains ----
-        float s[2][4], s2[2][4];
-#pragma unroll
-        for (int n = 0; n < 2; ++n)
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            s[n][r] = 0.f;
-            s2[n][r] = 0.f;
-          }
-        {
-          const int tok = (lane & 7) + ((lane >> 4) & 1) * 8;
-          const int chsel = (lane >> 3) & 1;
-#pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const int sub = ks >> 2;
-            const int ch = (ks & 3) * 2 + chsel;
-            const uint32_t addr = kbase + sub * kTileBytes + tok * 128 + ((ch ^ (tok & 7)) << 4);
-            uint32_t b0, b1, b2, b3;
-            ldmatrix_x4(b0, b1, b2, b3, addr);
-            uint32_t afr[4];
-            afr[0] = qa[ks][0];
-            afr[1] = GR == 2 ? qa[ks][1] : 0u;
-            afr[2] = qa[ks][GR];
-            afr[3] = GR == 2 ? qa[ks][GR + 1] : 0u;
-            if (ks & 1) {
-              Mma<T>::m16n8k16(s2[0], afr, b0, b1);
-              Mma<T>::m16n8k16(s2[1], afr, b2, b3);
-            } else {
-              Mma<T>::m16n8k16(s[0], afr, b0, b1);
-              Mma<T>::m16n8k16(s[1], afr, b2, b3);
-            }
-          }
-#pragma unroll
-          for (int n = 0; n < 2; ++n)
-#pragma unroll
-            for (int r = 0; r < 4; ++r) s[n][r] += s2[n][r];
-        }
-        // ---- online softmax per query row ----
-        float pv[2][4];
-#pragma unroll
-        for (int r = 0; r < GR; ++r) {
-          float x[4];
-          bool vld[4];
-#pragma unroll
-          for (int n = 0; n < 2; ++n)
-#pragma unroll
-            for (int i = 0; i < 2; ++i) {
-              const int tok = n * 8 + tq * 2 + i;
-              vld[n * 2 + i] = tok < ntok;
-              x[n * 2 + i] = vld[n * 2 + i] ? s[n][2 * r + i] * a.scale : neg_inf();
-            }
-          float pm = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 1));
-          pm = fmaxf(pm, __shfl_xor_sync(0xffffffffu, pm, 2));
-          const float mnew = fmaxf(m_run[r], pm);
-          float alpha = 1.f;
-          float p[4];
-          if (mnew == neg_inf()) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = 0.f;
-          } else {
-            alpha = (m_run[r] == neg_inf()) ? 0.f : softmax_exp(m_run[r] - mnew);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) p[i] = vld[i] ? softmax_exp(x[i] - mnew) : 0.f;
-          }
-          float rs = (p[0] + p[1]) + (p[2] + p[3]);
-          rs += __shfl_xor_sync(0xffffffffu, rs, 1);
-          rs += __shfl_xor_sync(0xffffffffu, rs, 2);
-          l_run[r] = l_run[r] * alpha + rs;
-          m_run[r] = mnew;
-#pragma unroll
-          for (int n = 0; n < kNT; ++n) {
-            o[n][2 * r] *= alpha;
-            o[n][2 * r + 1] *= alpha;
-          }
-          pv[0][2 * r] = p[0];
-          pv[0][2 * r + 1] = p[1];
-          pv[1][2 * r] = p[2];
-          pv[1][2 * r + 1] = p[3];
-        }
-        uint32_t pa[4];
-        pa[0] = Mma<T>::pack(pv[0][0], pv[0][1]);
-        pa[1] = GR == 2 ? Mma<T>::pack(pv[0][2], pv[0][3]) : 0u;
-        pa[2] = Mma<T>::pack(pv[1][0], pv[1][1]);
-        pa[3] = GR == 2 ? Mma<T>::pack(pv[1][2], pv[1][3]) : 0u;
-        // ---- O += P V ----
-        {
-          const int tok = (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int chsel = lane >> 4;
-#pragma unroll
-          for (int jp = 0; jp < D / 16; ++jp) {
-            const int nt = jp * 2;
-            const int sub = nt >> 3;
-            const int ch = (nt & 7) + chsel;
-            const uint32_t addr = vbase + sub * kTileBytes + tok * 128 + ((ch ^ (tok & 7)) << 4);
-            uint32_t b0, b1, b2, b3;
-            ldmatrix_x4_trans(b0, b1, b2, b3, addr);
-            if constexpr (GR == 2) {
-              Mma<T>::m16n8k16(o[nt], pa, b0, b1);
-              Mma<T>::m16n8k16(o[nt + 1], pa, b2, b3);
-            } else {
-              // rows 8..15 are padding: accumulate them into scratch registers
-              Mma<T>::m16n8k16(o[nt][0], o[nt][1], dummy[0], dummy[1], pa, b0, b1);
-              Mma<T>::m16n8k16(o[nt + 1][0], o[nt + 1][1], dummy[0], dummy[1], pa, b2, b3);
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (jj + kStages < nmine) {
-        fence_proxy_async_smem();
-        issue(jj + kStages);
-      }
-    }
-    gpage += nmine;
-    if (failed) {
-#pragma unroll
-      for (int r = 0; r < GR; ++r) {
-        m_run[r] = neg_inf();
-        l_run[r] = 0.f;
-      }
-    }
-    // The ring is reused as the warp-state buffer: wait for every warp.
-    __syncthreads();
-    constexpr int S = wb_stride<D>();
-#pragma unroll
-    for (int r = 0; r < GR; ++r) {
-      const int g = gq + 8 * r;
-#pragma unroll
-      for (int n = 0; n < kNT; ++n) {
-        float2 v2 = failed ? make_float2(0.f, 0.f) : make_float2(o[n][2 * r], o[n][2 * r + 1]);
-        *reinterpret_cast<float2*>(&wb_o[(w * kGP + g) * S + n * 8 + tq * 2]) = v2;
-      }
-      if (tq == 0) {
-        wb_ml[(w * kGP + g) * 2] = m_run[r];
-        wb_ml[(w * kGP + g) * 2 + 1] = l_run[r];
-      }
-    }
-    return !failed;
-  }
-};
-
-// ---------------------------------------------------------------------------
 // CUDA-core per-page step (fp32 or mixed dtypes); lane owns head_dim columns
 // d = lane + 32 i. Up to GM query heads per KV head.
 // ---------------------------------------------------------------------------
@@ -854,74 +598,6 @@ attend_kernel(const __grid_constant__ AttendArgs a) {
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn get_encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, []() {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  });
-  return fn;
-}
-
-// K or V pool as a 4-D tensor {D, Hkv, BS, NB}, box {64, 1, BS, 1}, 128 B swizzle.
-bool make_pool_map(CUtensorMap* map, const void* base, const KvView& kv) {
-  EncodeTiledFn enc = get_encode_fn();
-  if (!enc) return false;
-  const int eb = dtype_bytes(kv.dtype);
-  cuuint64_t dims[4] = {(cuuint64_t)kv.d, (cuuint64_t)kv.hkv, (cuuint64_t)kv.bs,
-                        (cuuint64_t)kv.num_blocks};
-  cuuint64_t strides[3] = {(cuuint64_t)kv.sh * eb, (cuuint64_t)kv.st * eb, (cuuint64_t)kv.sb * eb};
-  cuuint32_t box[4] = {64, 1, (cuuint32_t)kv.bs, 1};
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUtensorMapDataType dt = kv.dtype == CVSA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  CUresult r = enc(map, dt, 4, const_cast<void*>(base), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
-struct MapKey {
-  const void* p;
-  int dtype, d, hkv, bs, nb;
-  int64_t sb, st, sh;
-  bool operator==(const MapKey& o) const {
-    return p == o.p && dtype == o.dtype && d == o.d && hkv == o.hkv && bs == o.bs && nb == o.nb &&
-           sb == o.sb && st == o.st && sh == o.sh;
-  }
-};
-struct MapKeyHash {
-  size_t operator()(const MapKey& k) const {
-    return std::hash<const void*>()(k.p) ^ (size_t)k.nb * 1315423911u ^ (size_t)k.sb;
-  }
-};
-
-bool cached_pool_map(CUtensorMap* out, const void* base, const KvView& kv) {
-  static std::mutex mu;
-  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-  MapKey key{base, kv.dtype, kv.d, kv.hkv, kv.bs, kv.num_blocks, kv.sb, kv.st, kv.sh};
-  std::lock_guard<std::mutex> lock(mu);
-  auto itr = cache.find(key);
-  if (itr != cache.end()) {
-    *out = itr->second;
-    return true;
-  }
-  if (!make_pool_map(out, base, kv)) return false;
-  if (cache.size() > 4096) cache.clear();
-  cache.emplace(key, *out);
-  return true;
-}
-
 ItemCfg item_cfg(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense) {
   ItemCfg c;
   const int heads = q.B * kv.hkv;
@@ -943,13 +619,6 @@ ItemCfg item_cfg(const QView& q, const KvView& kv, int max_sel, bool recover, bo
   if ((recover || dense) && c.nc < 1) c.nc = 1;
   c.iph = c.nd + c.nc;
   return c;
-}
-
-bool use_mma(const QView& q, const KvView& kv) {
-  return (kv.dtype == CVSA_DTYPE_BF16 || kv.dtype == CVSA_DTYPE_F16) && q.dtype == kv.dtype &&
-         (kv.d == 64 || kv.d == 128 || kv.d == 256) && (q.hq / kv.hkv) <= 16 &&
-         ((kv.sh * 2) % 16 == 0) && ((kv.st * 2) % 16 == 0) && ((kv.sb * 2) % 16 == 0) &&
-         (reinterpret_cast<uintptr_t>(kv.k) % 16 == 0) && (reinterpret_cast<uintptr_t>(kv.v) % 16 == 0);
 }
 
 template <class Path, int D>
@@ -975,12 +644,6 @@ cudaError_t launch_path(const AttendArgs& a, int max_items, cudaStream_t s, bool
   if (grid > max_items) grid = max_items;
   if (grid < 1) grid = 1;
   return launch_k(attend_kernel<Path, D>, dim3(grid), dim3(kNW * 32), smem, s, pdl, a);
-}
-
-template <typename T, int D>
-cudaError_t dispatch_mma(const AttendArgs& a, int max_items, cudaStream_t s, bool pdl) {
-  if (a.G <= 8) return launch_path<MmaPath<T, D, 1>, D>(a, max_items, s, pdl);
-  return launch_path<MmaPath<T, D, 2>, D>(a, max_items, s, pdl);
 }
 
 template <typename T, typename TQ, int D>
@@ -1024,6 +687,7 @@ int attend_complement_chunk() { return kMaxItemPages; }
 
 size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, bool recover,
                               bool dense) {
+  if (stream_attend_eligible(q, kv)) return stream_attend_workspace_bytes(q, kv);
   const ItemCfg ic = item_cfg(q, kv, max_sel, recover, dense);
   const size_t slots = (size_t)q.B * kv.hkv * ic.iph;
   const int G = q.hq / kv.hkv;
@@ -1036,13 +700,9 @@ size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, boo
 
 cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& p, int max_sel,
                           cudaStream_t s, bool pdl) {
+  if (stream_attend_eligible(q, kv)) return launch_stream_attend(q, kv, p, max_sel, s, pdl);
   AttendArgs a;
   memset(&a, 0, sizeof(a));
-  const bool mma = use_mma(q, kv);
-  if (mma) {
-    if (!cached_pool_map(&a.kmap, kv.k, kv) || !cached_pool_map(&a.vmap, kv.v, kv))
-      return cudaErrorInvalidValue;
-  }
   a.q = q.q;
   a.k = kv.k;
   a.v = kv.v;
@@ -1113,22 +773,6 @@ cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& 
   // upper bound of the virtual item space (the grid never exceeds it)
   const int max_items = (int)slots;
 
-  if (mma) {
-    if (kv.dtype == CVSA_DTYPE_BF16) {
-      switch (kv.d) {
-        case 64: return dispatch_mma<__nv_bfloat16, 64>(a, max_items, s, pdl);
-        case 128: return dispatch_mma<__nv_bfloat16, 128>(a, max_items, s, pdl);
-        case 256: return dispatch_mma<__nv_bfloat16, 256>(a, max_items, s, pdl);
-      }
-    } else {
-      switch (kv.d) {
-        case 64: return dispatch_mma<__half, 64>(a, max_items, s, pdl);
-        case 128: return dispatch_mma<__half, 128>(a, max_items, s, pdl);
-        case 256: return dispatch_mma<__half, 256>(a, max_items, s, pdl);
-      }
-    }
-    return cudaErrorInvalidValue;
-  }
   switch (kv.dtype) {
     case CVSA_DTYPE_F32: return dispatch_simt_q<float>(a, q.dtype, kv.d, max_items, s, pdl);
     case CVSA_DTYPE_BF16: return dispatch_simt_q<__nv_bfloat16>(a, q.dtype, kv.d, max_items, s, pdl);

@@ -1,0 +1,1128 @@
+// Sparse paged decode over a balanced page stream: the decode-step attention
+// for bf16 / f16 KV (q in the same dtype) in a 16-byte-aligned pool.
+//
+// Restates:
+//   * cvsa/kernels/sparse_decode.py:424-500 (split decode over a page list:
+//     s = (q . k) * D^-0.5, online softmax, unnormalised (o, m, l)) and
+//     :15-132 (normalised output o / max(l, 1e-6));
+//   * cvsa/backend.py:819-842, exact recovery of a rejected head. The
+//     reference attends the selected pages (draft) and the remaining valid
+//     pages (complement, cvsa/kernels/coverage.py:31-96) separately and merges
+//     the two (coverage.py:274-326, o = (o_d s_d + o_c s_c) / max(l, 1e-6)).
+//     Draft and complement partition the valid pages, so the merged result is
+//     the softmax over all valid pages; a rejected head is attended over that
+//     set directly, which is the same quantity with one merge fewer;
+//   * recover_merge with an external draft: the complement only (selected
+//     pages skipped through a bitmap), merged with the given draft.
+//
+// Work decomposition. Every head (b, kv head) of the launch contributes w_h
+// pages to one flat stream: its selected pages (list heads), or all of its
+// valid pages (range heads: dense steps and rejected heads). The stream of
+// P = sum(w_h) pages is cut into gridDim.x equal contiguous ranges, one per
+// persistent CTA (one CTA per SM), so the load is balanced to one page
+// whatever the mix of lengths, selections and rejections.
+//
+// Inside a CTA, warp NC resolves the CTA's stream positions 32 at a time
+// (head by binary search over the shared-memory prefix of w_h, then the
+// selection entry and the block-table entry) into a shared-memory ring of
+// page descriptors, running ahead of the consumers. Consumer warp k
+// (0 <= k < NC) owns positions j with j % NC == k: it copies each page's K and
+// V rows of its KV head (16 tokens x head_dim, 16-byte cp.async, 128-byte
+// swizzled rows) into its own ring of S stages, S - 1 pages ahead of the one
+// it computes, and runs S = Q K^T and O += P V on mma.sync m16n8k16 (all G
+// query heads of the KV head packed into M) with the online softmax in
+// registers. Pages are gathered at 256-byte granularity from pages scattered
+// over the pool, which per-warp 16-byte copies serve at full rate where
+// one small TMA box per 64 columns would bound each SM by its TMA issue rate.
+// At the end of each head a consumer writes its state (o, m, l per query
+// row) into one of two shared-memory head slots; a merger warp (warp NC + 1)
+// merges the NC states of each head in warp order. A head that lies inside
+// one CTA's range is then finished by the merger; a head split across CTAs
+// is published as a partial (two slots per CTA: the CTA's first and last
+// head) and the last CTA to publish (global ticket, no spin) merges the
+// partials in CTA order. Merge orders are fixed, so results are deterministic
+// for a given device. Consumer warps issue no memory fences: a fence would
+// wait for their copies in flight.
+#include <climits>
+
+#include "cvsa_common.cuh"
+#include "cvsa_internal.h"
+#include "cvsa_launch.cuh"
+
+namespace cvsa {
+namespace {
+
+constexpr int kBS = 16;                  // tokens per page
+constexpr int kMaxChunkHeads = 2048;     // heads per launch (shared-memory head table)
+constexpr int kMaxConsumers = 8;
+constexpr int kMetaPerConsumer = 64;     // page descriptors in flight per consumer
+constexpr int kMaxStages = 8;            // per-consumer ring depth (cp.async.wait_group)
+constexpr int kSmemCap = 227 * 1024;     // dynamic shared memory per CTA on sm_100
+constexpr uint32_t kSpinLimit = 1u << 22;
+// the softmax reference max is refreshed when a score passes it by more than
+// this (natural log units): probabilities stay below e^8 ~ 3e3
+constexpr float kRescaleGap = 8.0f;
+
+enum : int { kKindEmpty = 0, kKindList = 1, kKindRange = 2, kKindRangeSkip = 3 };
+
+struct StreamArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  int64_t sb, st, sh;  // pool strides (elements): block, token, head
+  int B, hq, hkv, G, W, num_blocks;
+  const int32_t* tables;
+  const int32_t* lens;
+  const int32_t* sel0;
+  const int32_t* n0;
+  const int32_t* sel1;
+  const int32_t* n1;
+  int sel_stride;
+  int src_select;
+  const int32_t* decision;
+  int dense, recover, external_draft;
+  const uint8_t* accept;
+  const uint32_t* bitmap;
+  int bitmap_words;
+  const float* ext_o;
+  const float* ext_m;
+  const float* ext_l;
+  int commit;
+  int32_t* commit_idx;
+  int32_t* commit_n;
+  void* out;
+  int out_dtype;
+  float* o_unnorm;
+  float* m_out;
+  float* l_out;
+  int64_t* counters;
+  int32_t* dev_err;
+  uint8_t* accept_out;
+  float* cov_out;
+  const uint8_t* acc0;
+  const float* cov0;
+  const uint8_t* acc1;
+  const float* cov1;
+  float* part_o;       // [2 * gridDim.x][G][D]
+  float* part_ml;      // [2 * gridDim.x][G][2]
+  int32_t* head_done;  // per (b, kv head) of the whole call, zero at rest
+  int h_base, n_heads; // heads [h_base, h_base + n_heads) of this launch
+  int nc, stages, meta_cap;
+  // shared-memory carve-up, byte offsets from the 1024-aligned base
+  int off_flush, off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+  float scale;
+};
+
+// misc words
+constexpr int kMiscSlotCnt = 0;    // [2] consumers that flushed into head slot r
+constexpr int kMiscSlotDone = 2;   // [2] merges completed on slot r
+constexpr int kMiscFail = 4;       // a bounded wait gave up: stop
+constexpr int kMiscProd = 5;       // page descriptors published (local positions)
+constexpr int kMiscScan = 8;       // [33] block-scan scratch
+constexpr int kMiscCons = 48;      // [kMaxConsumers] next position each consumer reads
+constexpr int kMiscWts = 64;       // [16 * kMaxConsumers + 32] merger scratch
+constexpr int kMiscWords = kMiscWts + 16 * kMaxConsumers + 32;
+
+// Row stride (floats) of a head slot: D + 4 puts the 32 lanes' scalar
+// stores of one flush step (rows 2tq + i, columns gq) in distinct banks.
+template <int D>
+constexpr int flush_stride() { return D + 4; }
+
+// Consumer warps a launch may use: 8, or 4 where the wider per-lane state
+// (head_dim 256, or more than 8 query heads at head_dim 128) needs the larger
+// register budget of a smaller CTA.
+template <int D, int GR>
+constexpr int max_consumers() { return D == 64 ? kMaxConsumers : (D == 128 && GR == 1) ? 6 : 4; }
+
+__device__ __forceinline__ int block_excl_scan(int v, int* scratch, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) scratch[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int x = lane < nw ? scratch[lane] : 0;
+    int xi = x;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, xi, o);
+      if (lane >= o) xi += n;
+    }
+    if (lane < nw) scratch[lane] = xi - x;
+    if (lane == 31) scratch[32] = xi;
+  }
+  __syncthreads();
+  *total = scratch[32];
+  const int r = scratch[warp] + incl - v;
+  __syncthreads();
+  return r;
+}
+
+// Bounded spin (lane-local) until *w >= target; false if it gave up.
+__device__ __forceinline__ bool spin_until_ge(volatile int* w, int target, volatile int* fail) {
+  uint32_t it = 0;
+  while (*w < target) {
+    if (*fail) return false;
+    if (++it > kSpinLimit) return false;
+    __nanosleep(32);
+  }
+  return true;
+}
+
+template <int N>
+__device__ __forceinline__ void load_vec(const float* p, float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 t = *reinterpret_cast<const float4*>(p + i);
+      v[i] = t.x; v[i + 1] = t.y; v[i + 2] = t.z; v[i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+      const float2 t = *reinterpret_cast<const float2*>(p + i);
+      v[i] = t.x; v[i + 1] = t.y;
+    }
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void load_vec_cg(const float* p, float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4) {
+      const float4 t = __ldcg(reinterpret_cast<const float4*>(p + i));
+      v[i] = t.x; v[i + 1] = t.y; v[i + 2] = t.z; v[i + 3] = t.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+      const float2 t = __ldcg(reinterpret_cast<const float2*>(p + i));
+      v[i] = t.x; v[i + 1] = t.y;
+    }
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void store_vec_cg(float* p, const float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4)
+      __stcg(reinterpret_cast<float4*>(p + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 2)
+      __stcg(reinterpret_cast<float2*>(p + i), make_float2(v[i], v[i + 1]));
+  }
+}
+
+template <typename TO>
+__device__ __forceinline__ void store_o(void* out, int64_t idx, float v) {
+  reinterpret_cast<TO*>(out)[idx] = Elem<TO>::from_f(v);
+}
+
+__device__ __forceinline__ void store_out(void* out, int dt, int64_t idx, float v) {
+  if (dt == CVSA_DTYPE_BF16) store_o<__nv_bfloat16>(out, idx, v);
+  else if (dt == CVSA_DTYPE_F16) store_o<__half>(out, idx, v);
+  else store_o<float>(out, idx, v);
+}
+
+// Write the outputs of query row g of head bh from its merged state; lane
+// holds o[d] for the D/32 consecutive columns d = lane * D/32 + i.
+template <int D>
+__device__ __forceinline__ void finish_row(const StreamArgs& a, int bh, int kind, int g, float M,
+                                           float L, const float (&o)[D / 32]) {
+  constexpr int PL = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int b = bh / a.hkv, hh = bh % a.hkv;
+  const int64_t qrow = (int64_t)b * a.hq + (int64_t)hh * a.G + g;
+  const int64_t d0 = qrow * D + lane * PL;
+  if (a.o_unnorm) {
+#pragma unroll
+    for (int i = 0; i < PL; ++i) a.o_unnorm[d0 + i] = o[i];
+  }
+  if (lane == 0) {
+    if (a.m_out) a.m_out[qrow] = M;
+    if (a.l_out) a.l_out[qrow] = L;
+  }
+  if (!a.out) return;
+  if (a.external_draft) {
+    const float md = a.ext_m[qrow], ld = a.ext_l[qrow];
+    const bool merge = kind == kKindRangeSkip;
+    // coverage.py:318-326: merge draft and complement, divide by max(l, 1e-6)
+    const float m_all = merge ? fmaxf(md, M) : md;
+    const float sd = (md == neg_inf()) ? 0.f : expf(md - m_all);
+    const float sc = (!merge || M == neg_inf()) ? 0.f : expf(M - m_all);
+    const float lm = merge ? ld * sd + L * sc : ld;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const float od = a.ext_o[d0 + i];
+      const float r = merge ? (od * sd + o[i] * sc) / fmaxf(lm, 1e-6f) : od / fmaxf(ld, 1e-6f);
+      store_out(a.out, a.out_dtype, d0 + i, r);
+    }
+  } else {
+    const float inv = 1.0f / fmaxf(L, 1e-6f);
+#pragma unroll
+    for (int i = 0; i < PL; ++i) store_out(a.out, a.out_dtype, d0 + i, o[i] * inv);
+  }
+}
+
+template <typename T, int D, int GR>
+__global__ void __launch_bounds__((max_consumers<D, GR>() + 2) * 32, 1)
+stream_attend_kernel(const __grid_constant__ StreamArgs a) {
+  constexpr int kSub = D / 64;                         // 64-column slices
+  constexpr int kTile = kBS * 128;                     // one swizzled slice of a page
+  constexpr uint32_t kStageBytes = 2 * kSub * kTile;   // K and V of one page
+  constexpr int FS = flush_stride<D>();
+  constexpr int PL = D / 32;                           // merged columns per lane
+  constexpr int GP = 8 * GR;                           // query-row capacity
+  constexpr int kRowChunks = D / 8;                    // 16-byte chunks per token row
+  constexpr int kCopies = kBS * kRowChunks / 32;       // cp.async per lane per tensor and page
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* ring = sm;
+  float* flush = reinterpret_cast<float*>(sm + a.off_flush);
+  int2* meta = reinterpret_cast<int2*>(sm + a.off_meta);
+  int* stage_nt = reinterpret_cast<int*>(sm + a.off_snt);
+  int* pref = reinterpret_cast<int*>(sm + a.off_pref);
+  int* ctxv = reinterpret_cast<int*>(sm + a.off_ctx);
+  uint8_t* kindv = sm + a.off_kind;
+  uint32_t* span = reinterpret_cast<uint32_t*>(sm + a.off_span);  // first CTA << 16 | last CTA
+  int* misc = reinterpret_cast<int*>(sm + a.off_misc);
+  volatile int* vmisc = misc;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NC = a.nc, S = a.stages, H = a.n_heads, G = a.G, MR = a.meta_cap;
+  const int C = gridDim.x, c = blockIdx.x;
+  const int nthreads = blockDim.x;
+
+  for (int i = tid; i < kMiscWords; i += nthreads) misc[i] = 0;
+  pdl_wait();
+
+  // ---- head table: kind, context length and the exclusive prefix of w_h ----
+  int src = a.src_select;
+  if (src == 2) src = (a.decision[0] & 1) ? 0 : 1;
+  const int32_t* nsrc = src ? a.n1 : a.n0;
+  const int32_t* sel = src ? a.sel1 : a.sel0;
+  {
+    const int per = (H + nthreads - 1) / nthreads;
+    const int h0 = min(tid * per, H), h1 = min(h0 + per, H);
+    int sum = 0;
+    long long att = 0, mx = 0;
+    for (int h = h0; h < h1; ++h) {
+      const int bh = a.h_base + h;
+      const int ctx = a.lens[bh / a.hkv];
+      const int nv = min(n_valid_pages(ctx, kBS), a.W);
+      int kind, w;
+      if (a.dense) {
+        kind = kKindRange;
+        w = nv;
+        att += nv;
+      } else if (a.external_draft) {
+        const bool rej = a.recover && a.accept[bh] == 0;
+        kind = rej ? kKindRangeSkip : kKindEmpty;
+        w = rej ? nv : 0;
+      } else {
+        const int ns = min(max(nsrc[bh], 0), a.sel_stride);
+        const bool rej = a.recover && src == 1 && a.accept[bh] == 0;
+        kind = rej ? kKindRange : kKindList;
+        w = rej ? nv : ns;
+        att += rej ? max(ns, nv) : ns;
+      }
+      mx += nv;
+      ctxv[h] = ctx;
+      kindv[h] = (uint8_t)kind;
+      pref[h] = w;
+      sum += w;
+    }
+    if (c == 0 && a.counters) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        att += __shfl_xor_sync(0xffffffffu, att, o);
+        mx += __shfl_xor_sync(0xffffffffu, mx, o);
+      }
+      if (lane == 0) {
+        atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[CVSA_CTR_PAGES_ATTENDED]),
+                  (unsigned long long)att);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&a.counters[CVSA_CTR_PAGES_MAX]),
+                  (unsigned long long)mx);
+      }
+    }
+    int total = 0;
+    int base = block_excl_scan(sum, misc + kMiscScan, &total);
+    for (int h = h0; h < h1; ++h) {
+      const int w = pref[h];
+      pref[h] = base;
+      base += w;
+    }
+    if (tid == 0) pref[H] = total;
+  }
+  // committing the new selection and the gate of the decoded selection are
+  // per-head copies with no readers in this launch; spread them over CTAs
+  if ((a.commit && src == 1) || (a.accept_out && !a.dense)) {
+    for (int h = c; h < H; h += C) {
+      const int bh = a.h_base + h;
+      if (a.commit && src == 1) {
+        const int ns = min(max(a.n1[bh], 0), a.sel_stride);
+        const int64_t row = (int64_t)bh * a.sel_stride;
+        for (int i = tid; i < ns; i += nthreads) a.commit_idx[row + i] = a.sel1[row + i];
+        if (tid == 0) a.commit_n[bh] = ns;
+      }
+      if (tid == 0 && a.accept_out && !a.dense) {
+        const uint8_t* ga = src == 1 ? a.acc1 : a.acc0;
+        const float* gc = src == 1 ? a.cov1 : a.cov0;
+        a.accept_out[bh] = ga ? ga[bh] : 1;
+        if (a.cov_out) a.cov_out[bh] = gc ? gc[bh] : 1.f;
+      }
+    }
+  }
+  __syncthreads();
+
+  const int P = pref[H];
+  if (P == 0) {
+    // nothing to stream: every head is finished from the empty state
+    if (warp < NC) {
+      float o[PL];
+#pragma unroll
+      for (int i = 0; i < PL; ++i) o[i] = 0.f;
+      for (int h = c * NC + warp; h < H; h += C * NC)
+        for (int g = 0; g < G; ++g) finish_row<D>(a, a.h_base + h, kindv[h], g, neg_inf(), 0.f, o);
+    }
+    return;
+  }
+  const int Xc = (int)((long long)P * c / C);
+  const int Xe = (int)((long long)P * (c + 1) / C);
+  const int nloc = Xe - Xc;
+  // first / last CTA that works on each head (an empty head belongs to the
+  // CTA holding its position), computed once: CTA c holds stream positions
+  // [P c / C, P (c + 1) / C), so position x lies in CTA ((x + 1) C - 1) / P
+  {
+    auto cta_of = [&](int x) -> int { return (int)(((long long)(x + 1) * C - 1) / P); };
+    for (int h = tid; h < H; h += nthreads) {
+      const int s0 = pref[h], w = pref[h + 1] - s0;
+      const int f = s0 < P ? cta_of(s0) : C - 1;
+      const int l = w > 0 ? cta_of(s0 + w - 1) : f;
+      span[h] = ((uint32_t)f << 16) | (uint32_t)l;
+    }
+  }
+  __syncthreads();
+  auto first_cta = [&](int h) -> int { return (int)(span[h] >> 16); };
+  auto last_cta = [&](int h) -> int { return (int)(span[h] & 0xffffu); };
+  // this CTA's heads: [hlo, hhi]
+  int hlo, hhi;
+  {
+    int lo = 0, hi = H;  // first h with last_cta(h) >= c
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (last_cta(mid) >= c) hi = mid;
+      else lo = mid + 1;
+    }
+    hlo = lo;
+    lo = -1;
+    hi = H - 1;  // last h with first_cta(h) <= c
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (first_cta(mid) <= c) lo = mid;
+      else hi = mid - 1;
+    }
+    hhi = lo;
+  }
+
+  if (warp == NC) {
+    // ======================= page-descriptor producer =======================
+    for (int xb = 0; xb < nloc; xb += 32) {
+      const int p = xb + lane;  // local position
+      int blk = -1, nt = 0;
+      if (p < nloc) {
+        const int x = Xc + p;
+        int lo = 0, hi = H - 1;  // largest h with pref[h] <= x (a non-empty head)
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (pref[mid] <= x) lo = mid;
+          else hi = mid - 1;
+        }
+        const int h = lo;
+        const int i = x - pref[h];
+        const int bh = a.h_base + h;
+        const int kind = kindv[h];
+        int pg = i;
+        bool ok = true;
+        if (kind == kKindList) {
+          pg = sel[(int64_t)bh * a.sel_stride + i];
+          if (pg < 0 || pg >= a.W) {
+            set_dev_error(a.dev_err, CVSA_DEV_ERR_PAGE_RANGE);
+            ok = false;
+          }
+        } else if (kind == kKindRangeSkip) {
+          const uint32_t word = a.bitmap[(int64_t)bh * a.bitmap_words + (pg >> 5)];
+          ok = ((word >> (pg & 31)) & 1u) == 0;
+        }
+        if (ok) {
+          const int ntok = min(kBS, ctxv[h] - pg * kBS);
+          if (ntok > 0) {
+            const int bk = a.tables[(int64_t)(bh / a.hkv) * a.W + pg];
+            if (bk < 0 || bk >= a.num_blocks) {
+              set_dev_error(a.dev_err, CVSA_DEV_ERR_BLOCK_RANGE);
+            } else {
+              blk = bk;
+              nt = ntok | ((bh % a.hkv) << 8);
+            }
+          }
+        }
+        // the ring entry is free once its previous position has been read
+        if (p >= MR && !spin_until_ge(vmisc + kMiscCons + p % NC, p - MR + 1, vmisc + kMiscFail)) {
+          vmisc[kMiscFail] = 1;
+          set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
+        }
+        meta[p % MR] = make_int2(blk, nt);
+      }
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) vmisc[kMiscProd] = min(xb + 32, nloc);
+      if (vmisc[kMiscFail]) break;
+    }
+    return;
+  }
+
+  if (warp == NC + 1) {
+    // ================================ merger ================================
+    // Merges each head's NC consumer states (in warp order) and finishes the
+    // head, or publishes it when it is split across CTAs; this warp issues no
+    // copies, so its memory fences are cheap.
+    float* wts = reinterpret_cast<float*>(misc + kMiscWts);  // [16][8] weights, [16][2] (M, L)
+    for (int h = hlo, lt = 0; h <= hhi; ++h, ++lt) {
+      const int r = lt & 1;
+      const float* so = flush + (size_t)r * NC * G * (FS + 2);
+      const float* sml = so + (size_t)NC * G * FS;
+      if (lane == 0 && !spin_until_ge(vmisc + kMiscSlotCnt + r, NC, vmisc + kMiscFail)) {
+        vmisc[kMiscFail] = 1;
+        set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
+      }
+      __syncwarp();
+      if (vmisc[kMiscFail]) return;
+      const int bh = a.h_base + h;
+      const int fc = first_cta(h), lc = last_cta(h);
+      const bool split = fc != lc;
+      const int kind = kindv[h];
+      const int slot = (h == hlo) ? 2 * c : 2 * c + 1;
+      // lane g (< G): row g's maximum, the consumers' weights and the sum
+      if (lane < G) {
+        float M = neg_inf();
+        for (int kk = 0; kk < NC; ++kk) M = fmaxf(M, sml[(kk * G + lane) * 2]);
+        float L = 0.f;
+        for (int kk = 0; kk < NC; ++kk) {
+          const float mk = sml[(kk * G + lane) * 2];
+          const float wk = (mk == neg_inf()) ? 0.f : expf(mk - M);
+          wts[lane * kMaxConsumers + kk] = wk;
+          L += sml[(kk * G + lane) * 2 + 1] * wk;
+        }
+        wts[16 * kMaxConsumers + lane * 2] = M;
+        wts[16 * kMaxConsumers + lane * 2 + 1] = L;
+      }
+      __syncwarp();
+      for (int g = 0; g < G; ++g) {
+        const float M = wts[16 * kMaxConsumers + g * 2];
+        const float L = wts[16 * kMaxConsumers + g * 2 + 1];
+        float acc[PL];
+#pragma unroll
+        for (int i = 0; i < PL; ++i) acc[i] = 0.f;
+        for (int kk = 0; kk < NC; ++kk) {
+          const float w = wts[g * kMaxConsumers + kk];
+          float v[PL];
+          load_vec<PL>(&so[(kk * G + g) * FS + lane * PL], v);
+#pragma unroll
+          for (int i = 0; i < PL; ++i) acc[i] += w * v[i];
+        }
+        if (!split) {
+          finish_row<D>(a, bh, kind, g, M, L, acc);
+        } else {
+          store_vec_cg<PL>(a.part_o + ((int64_t)slot * G + g) * D + lane * PL, acc);
+          if (lane == 0) {
+            __stcg(&a.part_ml[((int64_t)slot * G + g) * 2], M);
+            __stcg(&a.part_ml[((int64_t)slot * G + g) * 2 + 1], L);
+          }
+        }
+      }
+      // the slot's states (and the weights) are read: release the slot to the
+      // next head that maps to it
+      __syncwarp();
+      if (lane == 0) {
+        misc[kMiscSlotCnt + r] = 0;
+        __threadfence_block();
+        vmisc[kMiscSlotDone + r] = (lt >> 1) + 1;
+      }
+      if (!split) continue;
+
+      // ---- split head: publish, take the ticket, the last CTA merges ----
+      __threadfence();
+      __syncwarp();
+      int last = 0;
+      if (lane == 0) {
+        last = atomicAdd(&a.head_done[bh], 1) == lc - fc ? 1 : 0;
+        if (last) __threadfence();
+      }
+      __syncwarp();
+      last = __shfl_sync(0xffffffffu, last, 0);
+      if (!last) continue;
+      const int np = lc - fc + 1;
+      // slot of contributor fc + t: its first head (2c) unless head h is not
+      // the first head of CTA fc (an earlier head also reaches into fc)
+      const bool fc_second = !(h == 0 || last_cta(h - 1) < fc);
+      auto slot_of = [&](int t) -> int64_t {
+        return (t == 0 && fc_second) ? 2 * fc + 1 : 2 * (fc + t);
+      };
+      // pass 1: per-row maximum over all partials (one load round)
+      float Mg[GP];
+#pragma unroll
+      for (int g = 0; g < GP; ++g) Mg[g] = neg_inf();
+      for (int t0 = 0; t0 < np; t0 += 32) {
+        const int t = t0 + lane;
+        if (t < np) {
+          const int64_t sl = slot_of(t);
+#pragma unroll
+          for (int g = 0; g < GP; ++g)
+            if (g < G) Mg[g] = fmaxf(Mg[g], __ldcg(&a.part_ml[(sl * G + g) * 2]));
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < GP; ++g) Mg[g] = warp_max(Mg[g]);
+      // pass 2: weights, sums and the weighted partial outputs
+      float Lg[GP];
+      float acc[GP][PL];
+#pragma unroll
+      for (int g = 0; g < GP; ++g) {
+        Lg[g] = 0.f;
+#pragma unroll
+        for (int i = 0; i < PL; ++i) acc[g][i] = 0.f;
+      }
+      for (int t0 = 0; t0 < np; t0 += 32) {
+        const int t = t0 + lane;
+        float wl[GP];
+#pragma unroll
+        for (int g = 0; g < GP; ++g) wl[g] = 0.f;
+        if (t < np) {
+          const int64_t sl = slot_of(t);
+#pragma unroll
+          for (int g = 0; g < GP; ++g) {
+            if (g < G) {
+              const float mp = __ldcg(&a.part_ml[(sl * G + g) * 2]);
+              const float lp = __ldcg(&a.part_ml[(sl * G + g) * 2 + 1]);
+              wl[g] = (mp == neg_inf()) ? 0.f : expf(mp - Mg[g]);
+              Lg[g] += lp * wl[g];
+            }
+          }
+        }
+        const int cnt = min(32, np - t0);
+        for (int u = 0; u < cnt; ++u) {
+          const int64_t sl = slot_of(t0 + u);
+#pragma unroll
+          for (int g = 0; g < GP; ++g) {
+            if (g < G) {
+              const float w = __shfl_sync(0xffffffffu, wl[g], u);
+              float v[PL];
+              load_vec_cg<PL>(a.part_o + (sl * G + g) * D + lane * PL, v);
+#pragma unroll
+              for (int i = 0; i < PL; ++i) acc[g][i] += w * v[i];
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < GP; ++g)
+        if (g < G) finish_row<D>(a, bh, kind, g, Mg[g], warp_sum(Lg[g]), acc[g]);
+      if (lane == 0) a.head_done[bh] = 0;
+    }
+    return;
+  }
+
+  // =============================== consumers ===============================
+  const int k = warp;
+  const int gq = lane >> 2, tq = lane & 3;
+  const uint64_t policy = make_evict_first_policy();
+  uint8_t* myring = ring + (size_t)k * S * kStageBytes;
+  int* mynt = stage_nt + k * S;
+  const T* Kp = reinterpret_cast<const T*>(a.k);
+  const T* Vp = reinterpret_cast<const T*>(a.v);
+  // lane's 16-byte chunk of copy r: token r * kTPI + lane / kRowChunks,
+  // chunk lane % kRowChunks (global offset), swizzled into its stage row
+  constexpr int kTPI = 32 / kRowChunks;  // tokens per copy instruction
+  const int64_t lane_goff = (int64_t)(lane / kRowChunks) * a.st + (lane % kRowChunks) * 8;
+  const int64_t step_goff = (int64_t)kTPI * a.st;
+  uint32_t soffs[kCopies];
+#pragma unroll
+  for (int r = 0; r < kCopies; ++r) {
+    const int t = r * kTPI + lane / kRowChunks, c16 = lane % kRowChunks;
+    soffs[r] = (c16 >> 3) * kTile + t * 128 + (((c16 & 7) ^ (t & 7)) << 4);
+  }
+
+  // copy the page of my q-th position into stage q % S (a group is committed
+  // even when nothing is copied, so group counting stays uniform); the
+  // descriptor is {block, tokens | kv head << 8}
+  auto issue = [&](int q) -> bool {
+    const int j = k + q * NC;
+    if (j < nloc) {
+      if (lane == 0 && !spin_until_ge(vmisc + kMiscProd, j + 1, vmisc + kMiscFail)) {
+        vmisc[kMiscFail] = 1;
+        set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
+      }
+      __syncwarp();
+      if (vmisc[kMiscFail]) return false;
+      const int2 e = meta[j % MR];
+      if (lane == 0) mynt[q % S] = e.y & 0xff;
+      if ((e.y & 0xff) > 0) {
+        const int hh = e.y >> 8;
+        const int64_t gbase = (int64_t)e.x * a.sb + (int64_t)hh * a.sh + lane_goff;
+        const T* kr = Kp + gbase;
+        const T* vr = Vp + gbase;
+        const uint32_t sbase = smem_u32(myring + (size_t)(q % S) * kStageBytes);
+#pragma unroll
+        for (int r = 0; r < kCopies; ++r) {
+          cp_async16(sbase + soffs[r], kr + r * step_goff, policy);
+          cp_async16(sbase + kSub * kTile + soffs[r], vr + r * step_goff, policy);
+        }
+      }
+      // the descriptor has been consumed (the copies above used it): hand its
+      // ring entry back to the producer
+      __syncwarp();
+      if (lane == 0) vmisc[kMiscCons + k] = j + NC;
+    }
+    cp_async_commit();
+    return true;
+  };
+
+  // Running state of the current head in the transposed layout: O^T
+  // (head_dim x query rows) as m16n8 accumulators, lane (gq, tq) holding
+  // columns d = 16 mt + gq (+8) of query rows g = 8 n + 2 tq (+1); the
+  // reference max m_use the state is scaled by (uniform over the 8 lanes of a
+  // row), this lane's own max of the row's scores and its share of the row
+  // sum (both combined over the lanes when the head is flushed).
+  float o[D / 16][GR][4];
+  float m_use[GR][2], m_loc[GR][2], l_part[GR][2];
+  uint32_t qb[D / 16][GR][2];
+  auto reset_state = [&]() {
+#pragma unroll
+    for (int mt = 0; mt < D / 16; ++mt)
+#pragma unroll
+      for (int n = 0; n < GR; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[mt][n][i] = 0.f;
+#pragma unroll
+    for (int n = 0; n < GR; ++n)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        m_use[n][i] = neg_inf();
+        m_loc[n][i] = neg_inf();
+        l_part[n][i] = 0.f;
+      }
+  };
+  // Q^T as the B operand of S^T = K Q^T: b0 = Q[g][16 ks + 2 tq ..], b1 = +8
+  auto load_q = [&](int h) {
+    const int bh = a.h_base + h;
+    const int b = bh / a.hkv, hh = bh % a.hkv;
+    const T* qp = reinterpret_cast<const T*>(a.q) + ((int64_t)b * a.hq + (int64_t)hh * G) * D;
+#pragma unroll
+    for (int n = 0; n < GR; ++n) {
+      const int g = n * 8 + gq;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t lo = 0, hi = 0;
+        if (g < G) {
+          lo = *reinterpret_cast<const uint32_t*>(qp + (int64_t)g * D + ks * 16 + tq * 2);
+          hi = *reinterpret_cast<const uint32_t*>(qp + (int64_t)g * D + ks * 16 + 8 + tq * 2);
+        }
+        qb[ks][n][0] = lo;
+        qb[ks][n][1] = hi;
+      }
+    }
+  };
+
+  // Flush the state of head h (local index lt) into head slot lt % 2 for the
+  // merger warp. Consumer warps keep copies in flight across heads, and a
+  // memory fence would wait for them, so the hand-off uses none: shared
+  // memory serves each warp's requests in issue order, so the slot writes
+  // (ordered among the lanes by __syncwarp) reach shared memory before the
+  // count that announces them, and the merger reads the slot only after it
+  // has seen the count. Returns false when a bounded wait gave up.
+  auto flush_head = [&](int lt) -> bool {
+    const int r = lt & 1;
+    float* so = flush + (size_t)r * NC * G * (FS + 2);
+    float* sml = so + (size_t)NC * G * FS;
+    if (lane == 0 && !spin_until_ge(vmisc + kMiscSlotDone + r, (lt >> 1), vmisc + kMiscFail)) {
+      vmisc[kMiscFail] = 1;
+      set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
+    }
+    __syncwarp();
+    if (vmisc[kMiscFail]) return false;
+#pragma unroll
+    for (int n = 0; n < GR; ++n)
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        const int g = n * 8 + tq * 2 + i;
+        // exact row max, and the state rescaled from m_use to it (f <= 1)
+        float mt_ = m_loc[n][i];
+        mt_ = fmaxf(mt_, __shfl_xor_sync(0xffffffffu, mt_, 4));
+        mt_ = fmaxf(mt_, __shfl_xor_sync(0xffffffffu, mt_, 8));
+        mt_ = fmaxf(mt_, __shfl_xor_sync(0xffffffffu, mt_, 16));
+        const float f = (m_use[n][i] == neg_inf()) ? 0.f : softmax_exp(m_use[n][i] - mt_);
+        float lsum = l_part[n][i];
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 4);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 8);
+        lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
+        if (g < G) {
+#pragma unroll
+          for (int mt = 0; mt < D / 16; ++mt) {
+            so[(k * G + g) * FS + mt * 16 + gq] = o[mt][n][i] * f;
+            so[(k * G + g) * FS + mt * 16 + gq + 8] = o[mt][n][2 + i] * f;
+          }
+          if (gq == 0) {
+            sml[(k * G + g) * 2] = mt_;
+            sml[(k * G + g) * 2 + 1] = lsum * f;
+          }
+        }
+      }
+    __syncwarp();
+    if (lane == 0) atomicAdd(&misc[kMiscSlotCnt + r], 1);
+    return true;
+  };
+
+  // ---- main loop over my positions ----
+  const int nmine = nloc > k ? (nloc - k + NC - 1) / NC : 0;
+  bool ok = true;
+  for (int q = 0; q < S - 1 && ok; ++q) ok = issue(q);
+  int h = hlo, lt = 0;
+  bool have_q = false;
+  reset_state();
+  for (int q = 0; q < nmine && ok; ++q) {
+    ok = issue(q + S - 1);
+    if (!ok) break;
+    const int x = Xc + k + q * NC;
+    while (x >= pref[h + 1]) {  // heads that end before x are done for me
+      if (!flush_head(lt)) { ok = false; break; }
+      ++h;
+      ++lt;
+      have_q = false;
+      reset_state();
+    }
+    if (!ok) break;
+    if (!have_q) {
+      load_q(h);
+      have_q = true;
+    }
+    cp_async_wait_dyn(S - 1);
+    __syncwarp();
+    const int st = q % S;
+    const int nt = mynt[st];
+    if (nt > 0) {
+      const uint32_t kbase = smem_u32(myring + (size_t)st * kStageBytes);
+      const uint32_t vbase = kbase + kSub * kTile;
+      // ---- S^T = K Q^T: M = the page's 16 tokens, N = query rows, two k-chains ----
+      float sa[GR][4], sb[GR][4];
+#pragma unroll
+      for (int n = 0; n < GR; ++n)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          sa[n][i] = 0.f;
+          sb[n][i] = 0.f;
+        }
+      {
+        const int tok = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int chsel = (lane >> 4) & 1;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const int sub = ks >> 2;
+          const int ch = (ks & 3) * 2 + chsel;
+          uint32_t af[4];
+          ldmatrix_x4(af[0], af[1], af[2], af[3],
+                      kbase + sub * kTile + tok * 128 + ((ch ^ (tok & 7)) << 4));
+#pragma unroll
+          for (int n = 0; n < GR; ++n) {
+            if (ks & 1) Mma<T>::m16n8k16(sb[n], af, qb[ks][n][0], qb[ks][n][1]);
+            else Mma<T>::m16n8k16(sa[n], af, qb[ks][n][0], qb[ks][n][1]);
+          }
+        }
+      }
+      // ---- online softmax: lane holds tokens gq, gq + 8 of rows 8n + 2tq (+1) ----
+      // p = exp(s - m_use). The reference max m_use is raised, and the state
+      // rescaled, only when a score passes it by more than kRescaleGap, so
+      // p <= e^kRescaleGap and most pages need neither the row-max shuffles
+      // nor the rescale; flush_head moves the state to the exact row max.
+      const bool v0 = gq < nt, v1 = gq + 8 < nt;
+      float xs[GR][4];
+      bool grow = false;
+#pragma unroll
+      for (int n = 0; n < GR; ++n)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float x0 = v0 ? (sa[n][i] + sb[n][i]) * a.scale : neg_inf();
+          const float x1 = v1 ? (sa[n][2 + i] + sb[n][2 + i]) * a.scale : neg_inf();
+          xs[n][i] = x0;
+          xs[n][2 + i] = x1;
+          const float lm = fmaxf(x0, x1);
+          m_loc[n][i] = fmaxf(m_loc[n][i], lm);
+          grow |= lm > m_use[n][i] + kRescaleGap;
+        }
+      if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+        for (int n = 0; n < GR; ++n)
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            float mx = fmaxf(xs[n][i], xs[n][2 + i]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mnew = fmaxf(m_use[n][i], mx);
+            if (mnew != m_use[n][i]) {
+              const float alpha =
+                  (m_use[n][i] == neg_inf()) ? 0.f : softmax_exp(m_use[n][i] - mnew);
+              l_part[n][i] *= alpha;
+#pragma unroll
+              for (int mt = 0; mt < D / 16; ++mt) {
+                o[mt][n][i] *= alpha;
+                o[mt][n][2 + i] *= alpha;
+              }
+              m_use[n][i] = mnew;
+            }
+          }
+      }
+      uint32_t pb[GR][2];
+#pragma unroll
+      for (int n = 0; n < GR; ++n) {
+        float p[4];
+#pragma unroll
+        for (int i = 0; i < 2; ++i) {
+          const float mu = m_use[n][i];
+          const float p0 = (mu == neg_inf() || !v0) ? 0.f : softmax_exp(xs[n][i] - mu);
+          const float p1 = (mu == neg_inf() || !v1) ? 0.f : softmax_exp(xs[n][2 + i] - mu);
+          l_part[n][i] += p0 + p1;
+          p[i] = p0;
+          p[2 + i] = p1;
+        }
+        // P^T as the B operand: transpose the 8x8 token-by-row fragments
+        pb[n][0] = movmatrix_trans(Mma<T>::pack(p[0], p[1]));
+        pb[n][1] = movmatrix_trans(Mma<T>::pack(p[2], p[3]));
+      }
+      // ---- O^T += V^T P^T: M = 16 head_dim columns per tile, K = the 16 tokens ----
+      {
+        const int tok = (lane & 7) + ((lane >> 4) & 1) * 8;
+        const int chsel = (lane >> 3) & 1;
+#pragma unroll
+        for (int mt = 0; mt < D / 16; ++mt) {
+          const int sub = mt >> 2;
+          const int ch = (mt & 3) * 2 + chsel;
+          uint32_t af[4];
+          ldmatrix_x4_trans(af[0], af[1], af[2], af[3],
+                            vbase + sub * kTile + tok * 128 + ((ch ^ (tok & 7)) << 4));
+#pragma unroll
+          for (int n = 0; n < GR; ++n) Mma<T>::m16n8k16(o[mt][n], af, pb[n][0], pb[n][1]);
+        }
+      }
+    }
+    __syncwarp();  // the stage is refilled by the next issue
+  }
+  // heads after my last position (and the current one) are done for me
+  for (; ok && h <= hhi; ++h, ++lt) {
+    if (!flush_head(lt)) ok = false;
+    reset_state();
+  }
+  // no copy may still be landing in shared memory when the warp exits
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct Plan {
+  int nc, stages, meta_cap, smem;
+  int off_flush, off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+};
+
+size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Shared-memory plan for a launch of n_heads heads: the consumer count and
+// per-consumer ring depth that keep the most pages in flight.
+bool make_plan(int D, int G, int n_heads, int max_nc, Plan* best) {
+  const size_t stage = (size_t)2 * (D / 64) * kBS * 128;
+  const size_t fs = (size_t)D + 4;  // flush_stride<D>()
+  bool found = false;
+  int best_score = 0;
+  for (int nc = max_nc; nc >= 2; --nc) {
+    Plan p;
+    const size_t flush = (size_t)2 * nc * G * (fs + 2) * 4;
+    const int meta_cap = kMetaPerConsumer * nc;
+    const size_t tail = up(flush, 16) + up((size_t)meta_cap * 8, 16) +
+                        up((size_t)nc * kMaxStages * 4, 16) + up((size_t)(n_heads + 1) * 4, 16) +
+                        up((size_t)n_heads * 4, 16) + up((size_t)n_heads, 16) +
+                        up((size_t)n_heads * 4, 16) + kMiscWords * 4;
+    const size_t avail = (size_t)kSmemCap - 1024;  // alignment slack of the dynamic base
+    if (avail <= tail) continue;
+    int stages = (int)((avail - tail) / (stage * nc));
+    if (stages > kMaxStages) stages = kMaxStages;
+    if (stages < 2) continue;
+    size_t off = (size_t)nc * stages * stage;
+    p.off_flush = (int)off; off += up(flush, 16);
+    p.off_meta = (int)off; off += up((size_t)meta_cap * 8, 16);
+    p.off_snt = (int)off; off += up((size_t)nc * stages * 4, 16);
+    p.off_pref = (int)off; off += up((size_t)(n_heads + 1) * 4, 16);
+    p.off_ctx = (int)off; off += up((size_t)n_heads * 4, 16);
+    p.off_kind = (int)off; off += up((size_t)n_heads, 16);
+    p.off_span = (int)off; off += up((size_t)n_heads * 4, 16);
+    p.off_misc = (int)off; off += kMiscWords * 4;
+    if (off + 1024 > (size_t)kSmemCap) continue;
+    p.nc = nc;
+    p.stages = stages;
+    p.meta_cap = meta_cap;
+    p.smem = (int)(off + 1024);
+    const int score = nc * stages;
+    if (!found || score > best_score) {
+      *best = p;
+      best_score = score;
+      found = true;
+    }
+  }
+  return found;
+}
+
+template <typename T, int D, int GR>
+cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
+  Plan pl;
+  if (!make_plan(D, a.G, a.n_heads, max_consumers<D, GR>(), &pl)) return cudaErrorInvalidValue;
+  a.nc = pl.nc;
+  a.stages = pl.stages;
+  a.meta_cap = pl.meta_cap;
+  a.off_flush = pl.off_flush;
+  a.off_meta = pl.off_meta;
+  a.off_snt = pl.off_snt;
+  a.off_pref = pl.off_pref;
+  a.off_ctx = pl.off_ctx;
+  a.off_kind = pl.off_kind;
+  a.off_span = pl.off_span;
+  a.off_misc = pl.off_misc;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    e = cudaFuncSetAttribute(stream_attend_kernel<T, D, GR>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemCap);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  return launch_k(stream_attend_kernel<T, D, GR>, dim3(num_sms()), dim3((pl.nc + 2) * 32),
+                  (size_t)pl.smem, s, pdl, a);
+}
+
+template <typename T>
+cudaError_t dispatch(StreamArgs& a, int d, cudaStream_t s, bool pdl) {
+  const bool g2 = a.G > 8;
+  switch (d) {
+    case 64: return g2 ? launch_typed<T, 64, 2>(a, s, pdl) : launch_typed<T, 64, 1>(a, s, pdl);
+    case 128: return g2 ? launch_typed<T, 128, 2>(a, s, pdl) : launch_typed<T, 128, 1>(a, s, pdl);
+    case 256: return g2 ? launch_typed<T, 256, 2>(a, s, pdl) : launch_typed<T, 256, 1>(a, s, pdl);
+  }
+  return cudaErrorInvalidValue;
+}
+
+int chunk_heads(const QView& q, int max_sel) {
+  // keep the stream length of one launch within int32
+  const long long per = (long long)(q.W > max_sel ? q.W : max_sel) + 1;
+  long long ch = (long long)INT_MAX / per;
+  if (ch > kMaxChunkHeads) ch = kMaxChunkHeads;
+  return ch < 1 ? 1 : (int)ch;
+}
+
+}  // namespace
+
+bool stream_attend_eligible(const QView& q, const KvView& kv) {
+  return (kv.dtype == CVSA_DTYPE_BF16 || kv.dtype == CVSA_DTYPE_F16) && q.dtype == kv.dtype &&
+         kv.bs == kBS && (kv.d == 64 || kv.d == 128 || kv.d == 256) && kv.hkv > 0 &&
+         q.hq % kv.hkv == 0 && (q.hq / kv.hkv) <= 16 && ((kv.sh * 2) % 16 == 0) &&
+         ((kv.st * 2) % 16 == 0) && ((kv.sb * 2) % 16 == 0) &&
+         (reinterpret_cast<uintptr_t>(kv.k) % 16 == 0) &&
+         (reinterpret_cast<uintptr_t>(kv.v) % 16 == 0);
+}
+
+size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv) {
+  const size_t G = (size_t)(q.hq / kv.hkv);
+  const size_t slots = (size_t)2 * num_sms();
+  return up(slots * G * kv.d * 4, 256) + up(slots * G * 2 * 4, 256);
+}
+
+cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendParams& p,
+                                 int max_sel, cudaStream_t s, bool pdl) {
+  StreamArgs a;
+  memset(&a, 0, sizeof(a));
+  const int heads = q.B * kv.hkv;
+  if (heads <= 0) return cudaSuccess;
+  if (heads > kMaxHeadsPerCall) return cudaErrorInvalidValue;
+  a.q = q.q;
+  a.k = kv.k;
+  a.v = kv.v;
+  a.sb = kv.sb;
+  a.st = kv.st;
+  a.sh = kv.sh;
+  a.B = q.B;
+  a.hq = q.hq;
+  a.hkv = kv.hkv;
+  a.G = q.hq / kv.hkv;
+  a.W = q.W;
+  a.num_blocks = kv.num_blocks;
+  a.tables = q.tables;
+  a.lens = q.lens;
+  a.sel0 = p.sel0;
+  a.n0 = p.n0;
+  a.sel1 = p.sel1;
+  a.n1 = p.n1;
+  a.sel_stride = p.sel_stride;
+  a.src_select = p.src_select;
+  a.decision = p.decision;
+  a.dense = p.dense ? 1 : 0;
+  a.recover = p.recover ? 1 : 0;
+  a.external_draft = p.external_draft ? 1 : 0;
+  a.accept = p.accept;
+  a.bitmap = p.bitmap;
+  a.bitmap_words = p.bitmap_words;
+  a.ext_o = p.ext_o;
+  a.ext_m = p.ext_m;
+  a.ext_l = p.ext_l;
+  a.commit = p.commit_src1 ? 1 : 0;
+  a.commit_idx = p.commit_idx;
+  a.commit_n = p.commit_n;
+  a.out = p.out;
+  a.out_dtype = p.out_dtype;
+  a.o_unnorm = p.o_unnorm;
+  a.m_out = p.m_out;
+  a.l_out = p.l_out;
+  a.counters = p.counters;
+  a.dev_err = p.dev_err;
+  a.accept_out = p.accept_out;
+  a.cov_out = p.cov_out;
+  a.acc0 = p.acc0;
+  a.cov0 = p.cov0;
+  a.acc1 = p.acc1;
+  a.cov1 = p.cov1;
+  a.head_done = p.head_done;
+  a.scale = 1.0f / sqrtf((float)kv.d);
+  const size_t need = stream_attend_workspace_bytes(q, kv);
+  if (p.partial_bytes < need) return cudaErrorInvalidValue;
+  const size_t slots = (size_t)2 * num_sms();
+  a.part_o = reinterpret_cast<float*>(p.partials);
+  a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.partials) +
+                                       up(slots * a.G * kv.d * 4, 256));
+  const int chunk = chunk_heads(q, p.dense ? 1 : max_sel);
+  for (int h0 = 0; h0 < heads; h0 += chunk) {
+    a.h_base = h0;
+    a.n_heads = heads - h0 < chunk ? heads - h0 : chunk;
+    cudaError_t e = kv.dtype == CVSA_DTYPE_BF16 ? dispatch<__nv_bfloat16>(a, kv.d, s, pdl)
+                                                : dispatch<__half>(a, kv.d, s, pdl);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace cvsa

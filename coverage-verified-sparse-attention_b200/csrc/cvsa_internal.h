@@ -149,6 +149,12 @@ cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& 
 bool attend_supported(const QView& q, const KvView& kv);
 int attend_complement_chunk();  // logical pages per complement item
 
+// ---- attend_stream.cu (bf16 / f16, TMA-able pools; launch_attend routes) ----
+bool stream_attend_eligible(const QView& q, const KvView& kv);
+size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv);
+cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendParams& p,
+                                 int max_sel, cudaStream_t s, bool pdl);
+
 // ---- merge.cu ----
 cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
                              const float* o_c, const float* m_c, const float* l_c,

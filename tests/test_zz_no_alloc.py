@@ -78,10 +78,12 @@ def test_noalloc_matches_workspace_decode_twice(cuda):
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
+    # fp32 KV takes the general-layout kernel, whose item scratch grows with
+    # the selection width (the bf16/f16 stream kernel's scratch does not)
     lib = _lib.load()
     B, Hkv, D = 64, 8, 128
-    q = torch.zeros((B, 32, D), dtype=torch.bfloat16, device=cuda)
-    k = torch.zeros((8, 16, Hkv, D), dtype=torch.bfloat16, device=cuda)
+    q = torch.zeros((B, 32, D), dtype=torch.float32, device=cuda)
+    k = torch.zeros((8, 16, Hkv, D), dtype=torch.float32, device=cuda)
     bt = torch.zeros((B, 8), dtype=torch.int32, device=cuda)
     cl = torch.full((B,), 128, dtype=torch.int32, device=cuda)
     K = 2048                                  # a selection far wider than the scratch allows
@@ -90,6 +92,6 @@ def test_noalloc_rejects_shapes_beyond_its_scratch(cuda):
     out = torch.empty_like(q)
     rc = lib.cvsa_sparse_decode_noalloc(_lib.query_desc(q, bt, cl), _lib.kv_desc(k, k),
                                         idx.data_ptr(), K, n.data_ptr(), None, None, None,
-                                        out.data_ptr(), _lib.DTYPE_BF16, _lib.stream_ptr(cuda))
+                                        out.data_ptr(), _lib.DTYPE_F32, _lib.stream_ptr(cuda))
     assert rc == _lib.ERR_UNSUPPORTED
     assert b"no-alloc scratch holds" in lib.cvsa_last_error()
