@@ -687,7 +687,8 @@ int attend_complement_chunk() { return kMaxItemPages; }
 
 size_t attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel, bool recover,
                               bool dense) {
-  if (stream_attend_eligible(q, kv)) return stream_attend_workspace_bytes(q, kv);
+  if (stream_attend_eligible(q, kv))
+    return stream_attend_workspace_bytes(q, kv, dense ? 1 : max_sel);
   const ItemCfg ic = item_cfg(q, kv, max_sel, recover, dense);
   const size_t slots = (size_t)q.B * kv.hkv * ic.iph;
   const int G = q.hq / kv.hkv;

@@ -35,14 +35,12 @@
 // over the pool, which per-warp 16-byte copies serve at full rate where
 // one small TMA box per 64 columns would bound each SM by its TMA issue rate.
 // At the end of each head a consumer writes its state (o, m, l per query
-// row) into one of two shared-memory head slots; a merger warp (warp NC + 1)
-// merges the NC states of each head in warp order. A head that lies inside
-// one CTA's range is then finished by the merger; a head split across CTAs
-// is published as a partial (two slots per CTA: the CTA's first and last
-// head) and the last CTA to publish (global ticket, no spin) merges the
-// partials in CTA order. Merge orders are fixed, so results are deterministic
-// for a given device. Consumer warps issue no memory fences: a fence would
-// wait for their copies in flight.
+// row, rescaled to the exact row max) to a global partial; consumer warps
+// issue no memory fences, which would wait for their copies in flight. A
+// combine kernel, launched behind with programmatic dependent launch, merges
+// each head's partials (from every consumer of every CTA that worked on it,
+// in CTA then warp order, so results are deterministic for a given device)
+// and writes the outputs.
 #include <climits>
 
 #include "cvsa_common.cuh"
@@ -103,36 +101,33 @@ struct StreamArgs {
   const float* cov0;
   const uint8_t* acc1;
   const float* cov1;
-  float* part_o;       // [2 * gridDim.x][G][D]
-  float* part_ml;      // [2 * gridDim.x][G][2]
-  int32_t* head_done;  // per (b, kv head) of the whole call, zero at rest
+  float* part_o;       // [slots][G][D] consumer partials of this launch
+  float* part_ml;      // [slots][G][2]
+  int32_t* head_poff;  // [n_heads] first partial slot of each head (written by CTA 0)
+  int32_t* head_pcnt;  // [n_heads] partials of each head
+  uint8_t* head_kind;  // [n_heads]
   int h_base, n_heads; // heads [h_base, h_base + n_heads) of this launch
   int nc, stages, meta_cap;
   // shared-memory carve-up, byte offsets from the 1024-aligned base
-  int off_flush, off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_poff, off_misc;
   float scale;
 };
 
 // misc words
-constexpr int kMiscSlotCnt = 0;    // [2] consumers that flushed into head slot r
-constexpr int kMiscSlotDone = 2;   // [2] merges completed on slot r
 constexpr int kMiscFail = 4;       // a bounded wait gave up: stop
 constexpr int kMiscProd = 5;       // page descriptors published (local positions)
 constexpr int kMiscScan = 8;       // [33] block-scan scratch
 constexpr int kMiscCons = 48;      // [kMaxConsumers] next position each consumer reads
-constexpr int kMiscWts = 64;       // [16 * kMaxConsumers + 32] merger scratch
-constexpr int kMiscWords = kMiscWts + 16 * kMaxConsumers + 32;
-
-// Row stride (floats) of a head slot: D + 4 puts the 32 lanes' scalar
-// stores of one flush step (rows 2tq + i, columns gq) in distinct banks.
-template <int D>
-constexpr int flush_stride() { return D + 4; }
+constexpr int kMiscWords = 64;
 
 // Consumer warps a launch may use: 8, or 4 where the wider per-lane state
 // (head_dim 256, or more than 8 query heads at head_dim 128) needs the larger
 // register budget of a smaller CTA.
 template <int D, int GR>
-constexpr int max_consumers() { return D == 64 ? kMaxConsumers : (D == 128 && GR == 1) ? 6 : 4; }
+constexpr int max_consumers() { return (D == 256 || (D == 128 && GR == 2)) ? 4 : kMaxConsumers; }
+constexpr int max_consumers_rt(int D, int G) {
+  return (D == 256 || (D == 128 && G > 8)) ? 4 : kMaxConsumers;
+}
 
 __device__ __forceinline__ int block_excl_scan(int v, int* scratch, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -171,6 +166,18 @@ __device__ __forceinline__ bool spin_until_ge(volatile int* w, int target, volat
     __nanosleep(32);
   }
   return true;
+}
+
+template <int N>
+__device__ __forceinline__ void store_vec(float* p, const float (&v)[N]) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < N; i += 4)
+      *reinterpret_cast<float4*>(p + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < N; i += 2) *reinterpret_cast<float2*>(p + i) = make_float2(v[i], v[i + 1]);
+  }
 }
 
 template <int N>
@@ -231,8 +238,42 @@ __device__ __forceinline__ void store_out(void* out, int dt, int64_t idx, float 
   else store_o<float>(out, idx, v);
 }
 
-// Write the outputs of query row g of head bh from its merged state; lane
-// holds o[d] for the D/32 consecutive columns d = lane * D/32 + i.
+// Store PL consecutive outputs of one row in the output dtype, vectorised
+// when the destination allows.
+template <int PL>
+__device__ __forceinline__ void store_row(void* out, int dt, int64_t idx, const float (&r)[PL]) {
+  if (dt == CVSA_DTYPE_F32) {
+    float* p = reinterpret_cast<float*>(out) + idx;
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && PL % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < PL; i += 4)
+        *reinterpret_cast<float4*>(p + i) = make_float4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < PL; ++i) p[i] = r[i];
+    }
+    return;
+  }
+  uint32_t w[PL / 2];
+#pragma unroll
+  for (int i = 0; i < PL / 2; ++i)
+    w[i] = dt == CVSA_DTYPE_BF16 ? Mma<__nv_bfloat16>::pack(r[2 * i], r[2 * i + 1])
+                                 : Mma<__half>::pack(r[2 * i], r[2 * i + 1]);
+  uint32_t* p = reinterpret_cast<uint32_t*>(reinterpret_cast<uint16_t*>(out) + idx);
+  if ((reinterpret_cast<uintptr_t>(p) & 7) == 0 && PL % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < PL / 2; i += 2) *reinterpret_cast<uint2*>(p + i) = make_uint2(w[i], w[i + 1]);
+  } else if ((reinterpret_cast<uintptr_t>(p) & 3) == 0) {
+#pragma unroll
+    for (int i = 0; i < PL / 2; ++i) p[i] = w[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < PL; ++i) store_out(out, dt, idx + i, r[i]);
+  }
+}
+
+// Write the outputs of query row g of head bh from its merged state (M, L, o);
+// lane holds o[d] for the D/32 consecutive columns d = lane * D/32 + i.
 template <int D>
 __device__ __forceinline__ void finish_row(const StreamArgs& a, int bh, int kind, int g, float M,
                                            float L, const float (&o)[D / 32]) {
@@ -250,6 +291,7 @@ __device__ __forceinline__ void finish_row(const StreamArgs& a, int bh, int kind
     if (a.l_out) a.l_out[qrow] = L;
   }
   if (!a.out) return;
+  float r[PL];
   if (a.external_draft) {
     const float md = a.ext_m[qrow], ld = a.ext_l[qrow];
     const bool merge = kind == kKindRangeSkip;
@@ -257,42 +299,39 @@ __device__ __forceinline__ void finish_row(const StreamArgs& a, int bh, int kind
     const float m_all = merge ? fmaxf(md, M) : md;
     const float sd = (md == neg_inf()) ? 0.f : expf(md - m_all);
     const float sc = (!merge || M == neg_inf()) ? 0.f : expf(M - m_all);
-    const float lm = merge ? ld * sd + L * sc : ld;
+    const float lm = fmaxf(merge ? ld * sd + L * sc : ld, 1e-6f);
 #pragma unroll
     for (int i = 0; i < PL; ++i) {
       const float od = a.ext_o[d0 + i];
-      const float r = merge ? (od * sd + o[i] * sc) / fmaxf(lm, 1e-6f) : od / fmaxf(ld, 1e-6f);
-      store_out(a.out, a.out_dtype, d0 + i, r);
+      r[i] = merge ? (od * sd + o[i] * sc) / lm : od / lm;
     }
   } else {
-    const float inv = 1.0f / fmaxf(L, 1e-6f);
+    const float lm = fmaxf(L, 1e-6f);
 #pragma unroll
-    for (int i = 0; i < PL; ++i) store_out(a.out, a.out_dtype, d0 + i, o[i] * inv);
+    for (int i = 0; i < PL; ++i) r[i] = o[i] / lm;
   }
+  store_row<PL>(a.out, a.out_dtype, d0, r);
 }
 
 template <typename T, int D, int GR>
-__global__ void __launch_bounds__((max_consumers<D, GR>() + 2) * 32, 1)
+__global__ void __launch_bounds__((max_consumers<D, GR>() + 1) * 32, 1)
 stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   constexpr int kSub = D / 64;                         // 64-column slices
   constexpr int kTile = kBS * 128;                     // one swizzled slice of a page
   constexpr uint32_t kStageBytes = 2 * kSub * kTile;   // K and V of one page
-  constexpr int FS = flush_stride<D>();
-  constexpr int PL = D / 32;                           // merged columns per lane
-  constexpr int GP = 8 * GR;                           // query-row capacity
   constexpr int kRowChunks = D / 8;                    // 16-byte chunks per token row
   constexpr int kCopies = kBS * kRowChunks / 32;       // cp.async per lane per tensor and page
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* ring = sm;
-  float* flush = reinterpret_cast<float*>(sm + a.off_flush);
   int2* meta = reinterpret_cast<int2*>(sm + a.off_meta);
   int* stage_nt = reinterpret_cast<int*>(sm + a.off_snt);
   int* pref = reinterpret_cast<int*>(sm + a.off_pref);
   int* ctxv = reinterpret_cast<int*>(sm + a.off_ctx);
   uint8_t* kindv = sm + a.off_kind;
   uint32_t* span = reinterpret_cast<uint32_t*>(sm + a.off_span);  // first CTA << 16 | last CTA
+  int* poff = reinterpret_cast<int*>(sm + a.off_poff);  // first partial slot of each head
   int* misc = reinterpret_cast<int*>(sm + a.off_misc);
   volatile int* vmisc = misc;
 
@@ -305,17 +344,18 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   pdl_wait();
 
   // ---- head table: kind, context length and the exclusive prefix of w_h ----
-  int src = a.src_select;
-  if (src == 2) src = (a.decision[0] & 1) ? 0 : 1;
-  const int32_t* nsrc = src ? a.n1 : a.n0;
-  const int32_t* sel = src ? a.sel1 : a.sel0;
+  // (the decision word and both candidate counts are loaded together)
+  const int dec = a.src_select == 2 ? a.decision[0] : 0;
   {
     const int per = (H + nthreads - 1) / nthreads;
     const int h0 = min(tid * per, H), h1 = min(h0 + per, H);
     int sum = 0;
     long long att = 0, mx = 0;
+    const int src = a.src_select == 2 ? ((dec & 1) ? 0 : 1) : a.src_select;
     for (int h = h0; h < h1; ++h) {
       const int bh = a.h_base + h;
+      const int n0v = a.n0 ? a.n0[bh] : 0;
+      const int n1v = a.n1 ? a.n1[bh] : 0;
       const int ctx = a.lens[bh / a.hkv];
       const int nv = min(n_valid_pages(ctx, kBS), a.W);
       int kind, w;
@@ -328,7 +368,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
         kind = rej ? kKindRangeSkip : kKindEmpty;
         w = rej ? nv : 0;
       } else {
-        const int ns = min(max(nsrc[bh], 0), a.sel_stride);
+        const int ns = min(max(src ? n1v : n0v, 0), a.sel_stride);
         const bool rej = a.recover && src == 1 && a.accept[bh] == 0;
         kind = rej ? kKindRange : kKindList;
         w = rej ? nv : ns;
@@ -362,39 +402,32 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     }
     if (tid == 0) pref[H] = total;
   }
-  // committing the new selection and the gate of the decoded selection are
-  // per-head copies with no readers in this launch; spread them over CTAs
-  if ((a.commit && src == 1) || (a.accept_out && !a.dense)) {
+  __syncthreads();
+  const int src = a.src_select == 2 ? ((dec & 1) ? 0 : 1) : a.src_select;
+  const int32_t* sel = src ? a.sel1 : a.sel0;
+  // Committing the new selection and the gate of the decoded selection are
+  // per-head copies with no readers in this launch: the producer warp does
+  // them (spread over CTAs) once its descriptors are out.
+  auto commit_heads = [&]() {
+    if (!((a.commit && src == 1) || (a.accept_out && !a.dense))) return;
     for (int h = c; h < H; h += C) {
       const int bh = a.h_base + h;
       if (a.commit && src == 1) {
         const int ns = min(max(a.n1[bh], 0), a.sel_stride);
         const int64_t row = (int64_t)bh * a.sel_stride;
-        for (int i = tid; i < ns; i += nthreads) a.commit_idx[row + i] = a.sel1[row + i];
-        if (tid == 0) a.commit_n[bh] = ns;
+        for (int i = lane; i < ns; i += 32) a.commit_idx[row + i] = a.sel1[row + i];
+        if (lane == 0) a.commit_n[bh] = ns;
       }
-      if (tid == 0 && a.accept_out && !a.dense) {
+      if (lane == 0 && a.accept_out && !a.dense) {
         const uint8_t* ga = src == 1 ? a.acc1 : a.acc0;
         const float* gc = src == 1 ? a.cov1 : a.cov0;
         a.accept_out[bh] = ga ? ga[bh] : 1;
         if (a.cov_out) a.cov_out[bh] = gc ? gc[bh] : 1.f;
       }
     }
-  }
-  __syncthreads();
+  };
 
   const int P = pref[H];
-  if (P == 0) {
-    // nothing to stream: every head is finished from the empty state
-    if (warp < NC) {
-      float o[PL];
-#pragma unroll
-      for (int i = 0; i < PL; ++i) o[i] = 0.f;
-      for (int h = c * NC + warp; h < H; h += C * NC)
-        for (int g = 0; g < G; ++g) finish_row<D>(a, a.h_base + h, kindv[h], g, neg_inf(), 0.f, o);
-    }
-    return;
-  }
   const int Xc = (int)((long long)P * c / C);
   const int Xe = (int)((long long)P * (c + 1) / C);
   const int nloc = Xe - Xc;
@@ -413,6 +446,37 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   __syncthreads();
   auto first_cta = [&](int h) -> int { return (int)(span[h] >> 16); };
   auto last_cta = [&](int h) -> int { return (int)(span[h] & 0xffffu); };
+  // partial slots: every consumer of every CTA that works on a non-empty head
+  // writes one, at poff[h] + (c - first CTA) * NC + consumer
+  {
+    const int per = (H + nthreads - 1) / nthreads;
+    const int h0 = min(tid * per, H), h1 = min(h0 + per, H);
+    int sum = 0;
+    for (int h = h0; h < h1; ++h) {
+      const int n = pref[h + 1] > pref[h] ? (last_cta(h) - first_cta(h) + 1) * NC : 0;
+      poff[h] = n;
+      sum += n;
+    }
+    int total = 0;
+    int base = block_excl_scan(sum, misc + kMiscScan, &total);
+    for (int h = h0; h < h1; ++h) {
+      const int n = poff[h];
+      poff[h] = base;
+      if (c == 0) {
+        a.head_poff[h] = base;
+        a.head_pcnt[h] = n;
+        a.head_kind[h] = kindv[h];
+      }
+      base += n;
+    }
+  }
+  __syncthreads();
+  // let the combine kernel's CTAs be scheduled as this grid drains
+  pdl_launch_dependents();
+  if (P == 0) {
+    if (warp == NC) commit_heads();
+    return;
+  }
   // this CTA's heads: [hlo, hhi]
   int hlo, hhi;
   {
@@ -486,157 +550,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
       if (lane == 0) vmisc[kMiscProd] = min(xb + 32, nloc);
       if (vmisc[kMiscFail]) break;
     }
-    return;
-  }
-
-  if (warp == NC + 1) {
-    // ================================ merger ================================
-    // Merges each head's NC consumer states (in warp order) and finishes the
-    // head, or publishes it when it is split across CTAs; this warp issues no
-    // copies, so its memory fences are cheap.
-    float* wts = reinterpret_cast<float*>(misc + kMiscWts);  // [16][8] weights, [16][2] (M, L)
-    for (int h = hlo, lt = 0; h <= hhi; ++h, ++lt) {
-      const int r = lt & 1;
-      const float* so = flush + (size_t)r * NC * G * (FS + 2);
-      const float* sml = so + (size_t)NC * G * FS;
-      if (lane == 0 && !spin_until_ge(vmisc + kMiscSlotCnt + r, NC, vmisc + kMiscFail)) {
-        vmisc[kMiscFail] = 1;
-        set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
-      }
-      __syncwarp();
-      if (vmisc[kMiscFail]) return;
-      const int bh = a.h_base + h;
-      const int fc = first_cta(h), lc = last_cta(h);
-      const bool split = fc != lc;
-      const int kind = kindv[h];
-      const int slot = (h == hlo) ? 2 * c : 2 * c + 1;
-      // lane g (< G): row g's maximum, the consumers' weights and the sum
-      if (lane < G) {
-        float M = neg_inf();
-        for (int kk = 0; kk < NC; ++kk) M = fmaxf(M, sml[(kk * G + lane) * 2]);
-        float L = 0.f;
-        for (int kk = 0; kk < NC; ++kk) {
-          const float mk = sml[(kk * G + lane) * 2];
-          const float wk = (mk == neg_inf()) ? 0.f : expf(mk - M);
-          wts[lane * kMaxConsumers + kk] = wk;
-          L += sml[(kk * G + lane) * 2 + 1] * wk;
-        }
-        wts[16 * kMaxConsumers + lane * 2] = M;
-        wts[16 * kMaxConsumers + lane * 2 + 1] = L;
-      }
-      __syncwarp();
-      for (int g = 0; g < G; ++g) {
-        const float M = wts[16 * kMaxConsumers + g * 2];
-        const float L = wts[16 * kMaxConsumers + g * 2 + 1];
-        float acc[PL];
-#pragma unroll
-        for (int i = 0; i < PL; ++i) acc[i] = 0.f;
-        for (int kk = 0; kk < NC; ++kk) {
-          const float w = wts[g * kMaxConsumers + kk];
-          float v[PL];
-          load_vec<PL>(&so[(kk * G + g) * FS + lane * PL], v);
-#pragma unroll
-          for (int i = 0; i < PL; ++i) acc[i] += w * v[i];
-        }
-        if (!split) {
-          finish_row<D>(a, bh, kind, g, M, L, acc);
-        } else {
-          store_vec_cg<PL>(a.part_o + ((int64_t)slot * G + g) * D + lane * PL, acc);
-          if (lane == 0) {
-            __stcg(&a.part_ml[((int64_t)slot * G + g) * 2], M);
-            __stcg(&a.part_ml[((int64_t)slot * G + g) * 2 + 1], L);
-          }
-        }
-      }
-      // the slot's states (and the weights) are read: release the slot to the
-      // next head that maps to it
-      __syncwarp();
-      if (lane == 0) {
-        misc[kMiscSlotCnt + r] = 0;
-        __threadfence_block();
-        vmisc[kMiscSlotDone + r] = (lt >> 1) + 1;
-      }
-      if (!split) continue;
-
-      // ---- split head: publish, take the ticket, the last CTA merges ----
-      __threadfence();
-      __syncwarp();
-      int last = 0;
-      if (lane == 0) {
-        last = atomicAdd(&a.head_done[bh], 1) == lc - fc ? 1 : 0;
-        if (last) __threadfence();
-      }
-      __syncwarp();
-      last = __shfl_sync(0xffffffffu, last, 0);
-      if (!last) continue;
-      const int np = lc - fc + 1;
-      // slot of contributor fc + t: its first head (2c) unless head h is not
-      // the first head of CTA fc (an earlier head also reaches into fc)
-      const bool fc_second = !(h == 0 || last_cta(h - 1) < fc);
-      auto slot_of = [&](int t) -> int64_t {
-        return (t == 0 && fc_second) ? 2 * fc + 1 : 2 * (fc + t);
-      };
-      // pass 1: per-row maximum over all partials (one load round)
-      float Mg[GP];
-#pragma unroll
-      for (int g = 0; g < GP; ++g) Mg[g] = neg_inf();
-      for (int t0 = 0; t0 < np; t0 += 32) {
-        const int t = t0 + lane;
-        if (t < np) {
-          const int64_t sl = slot_of(t);
-#pragma unroll
-          for (int g = 0; g < GP; ++g)
-            if (g < G) Mg[g] = fmaxf(Mg[g], __ldcg(&a.part_ml[(sl * G + g) * 2]));
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < GP; ++g) Mg[g] = warp_max(Mg[g]);
-      // pass 2: weights, sums and the weighted partial outputs
-      float Lg[GP];
-      float acc[GP][PL];
-#pragma unroll
-      for (int g = 0; g < GP; ++g) {
-        Lg[g] = 0.f;
-#pragma unroll
-        for (int i = 0; i < PL; ++i) acc[g][i] = 0.f;
-      }
-      for (int t0 = 0; t0 < np; t0 += 32) {
-        const int t = t0 + lane;
-        float wl[GP];
-#pragma unroll
-        for (int g = 0; g < GP; ++g) wl[g] = 0.f;
-        if (t < np) {
-          const int64_t sl = slot_of(t);
-#pragma unroll
-          for (int g = 0; g < GP; ++g) {
-            if (g < G) {
-              const float mp = __ldcg(&a.part_ml[(sl * G + g) * 2]);
-              const float lp = __ldcg(&a.part_ml[(sl * G + g) * 2 + 1]);
-              wl[g] = (mp == neg_inf()) ? 0.f : expf(mp - Mg[g]);
-              Lg[g] += lp * wl[g];
-            }
-          }
-        }
-        const int cnt = min(32, np - t0);
-        for (int u = 0; u < cnt; ++u) {
-          const int64_t sl = slot_of(t0 + u);
-#pragma unroll
-          for (int g = 0; g < GP; ++g) {
-            if (g < G) {
-              const float w = __shfl_sync(0xffffffffu, wl[g], u);
-              float v[PL];
-              load_vec_cg<PL>(a.part_o + (sl * G + g) * D + lane * PL, v);
-#pragma unroll
-              for (int i = 0; i < PL; ++i) acc[g][i] += w * v[i];
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int g = 0; g < GP; ++g)
-        if (g < G) finish_row<D>(a, bh, kind, g, Mg[g], warp_sum(Lg[g]), acc[g]);
-      if (lane == 0) a.head_done[bh] = 0;
-    }
+    commit_heads();
     return;
   }
 
@@ -741,60 +655,46 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     }
   };
 
-  // Flush the state of head h (local index lt) into head slot lt % 2 for the
-  // merger warp. Consumer warps keep copies in flight across heads, and a
-  // memory fence would wait for them, so the hand-off uses none: shared
-  // memory serves each warp's requests in issue order, so the slot writes
-  // (ordered among the lanes by __syncwarp) reach shared memory before the
-  // count that announces them, and the merger reads the slot only after it
-  // has seen the count. Returns false when a bounded wait gave up.
-  auto flush_head = [&](int lt) -> bool {
-    const int r = lt & 1;
-    float* so = flush + (size_t)r * NC * G * (FS + 2);
-    float* sml = so + (size_t)NC * G * FS;
-    if (lane == 0 && !spin_until_ge(vmisc + kMiscSlotDone + r, (lt >> 1), vmisc + kMiscFail)) {
-      vmisc[kMiscFail] = 1;
-      set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
-    }
-    __syncwarp();
-    if (vmisc[kMiscFail]) return false;
+  // Write the state of head h as this consumer's partial, rescaled from the
+  // reference max m_use to the exact row max (f <= 1). Empty heads have no
+  // partials (the combine kernel finishes them from the empty state).
+  auto flush_head = [&](int h) {
+    if (pref[h + 1] == pref[h]) return;
+    const int64_t slot = poff[h] + (c - first_cta(h)) * NC + k;
 #pragma unroll
     for (int n = 0; n < GR; ++n)
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
         const int g = n * 8 + tq * 2 + i;
-        // exact row max, and the state rescaled from m_use to it (f <= 1)
-        float mt_ = m_loc[n][i];
-        mt_ = fmaxf(mt_, __shfl_xor_sync(0xffffffffu, mt_, 4));
-        mt_ = fmaxf(mt_, __shfl_xor_sync(0xffffffffu, mt_, 8));
-        mt_ = fmaxf(mt_, __shfl_xor_sync(0xffffffffu, mt_, 16));
-        const float f = (m_use[n][i] == neg_inf()) ? 0.f : softmax_exp(m_use[n][i] - mt_);
+        float mx = m_loc[n][i];
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float f = (m_use[n][i] == neg_inf()) ? 0.f : softmax_exp(m_use[n][i] - mx);
         float lsum = l_part[n][i];
         lsum += __shfl_xor_sync(0xffffffffu, lsum, 4);
         lsum += __shfl_xor_sync(0xffffffffu, lsum, 8);
         lsum += __shfl_xor_sync(0xffffffffu, lsum, 16);
         if (g < G) {
+          float* po = a.part_o + (slot * G + g) * D;
 #pragma unroll
           for (int mt = 0; mt < D / 16; ++mt) {
-            so[(k * G + g) * FS + mt * 16 + gq] = o[mt][n][i] * f;
-            so[(k * G + g) * FS + mt * 16 + gq + 8] = o[mt][n][2 + i] * f;
+            __stcg(&po[mt * 16 + gq], o[mt][n][i] * f);
+            __stcg(&po[mt * 16 + gq + 8], o[mt][n][2 + i] * f);
           }
           if (gq == 0) {
-            sml[(k * G + g) * 2] = mt_;
-            sml[(k * G + g) * 2 + 1] = lsum * f;
+            __stcg(&a.part_ml[(slot * G + g) * 2], mx);
+            __stcg(&a.part_ml[(slot * G + g) * 2 + 1], lsum * f);
           }
         }
       }
-    __syncwarp();
-    if (lane == 0) atomicAdd(&misc[kMiscSlotCnt + r], 1);
-    return true;
   };
 
   // ---- main loop over my positions ----
   const int nmine = nloc > k ? (nloc - k + NC - 1) / NC : 0;
   bool ok = true;
   for (int q = 0; q < S - 1 && ok; ++q) ok = issue(q);
-  int h = hlo, lt = 0;
+  int h = hlo;
   bool have_q = false;
   reset_state();
   for (int q = 0; q < nmine && ok; ++q) {
@@ -802,13 +702,11 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     if (!ok) break;
     const int x = Xc + k + q * NC;
     while (x >= pref[h + 1]) {  // heads that end before x are done for me
-      if (!flush_head(lt)) { ok = false; break; }
+      flush_head(h);
       ++h;
-      ++lt;
       have_q = false;
       reset_state();
     }
-    if (!ok) break;
     if (!have_q) {
       load_q(h);
       have_q = true;
@@ -925,8 +823,8 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     __syncwarp();  // the stage is refilled by the next issue
   }
   // heads after my last position (and the current one) are done for me
-  for (; ok && h <= hhi; ++h, ++lt) {
-    if (!flush_head(lt)) ok = false;
+  for (; ok && h <= hhi; ++h) {
+    flush_head(h);
     reset_state();
   }
   // no copy may still be landing in shared memory when the warp exits
@@ -934,43 +832,104 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
 }
 
 // ---------------------------------------------------------------------------
+// combine: one warp per (head, query row)
+// ---------------------------------------------------------------------------
+// Merges the head's consumer partials in slot order (CTA, then consumer) and
+// writes the outputs; a head without partials is finished from the empty
+// state. Restates the split-decode reduction of
+// cvsa/kernels/sparse_decode.py:577-606 (max over partials, weights
+// exp(m_i - M), sums) at warp scale.
+template <int D>
+__global__ void __launch_bounds__(256) stream_combine_kernel(const __grid_constant__ StreamArgs a) {
+  constexpr int PL = D / 32;
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int nw = (gridDim.x * blockDim.x) >> 5;
+  const int G = a.G;
+  for (int u = wg; u < a.n_heads * G; u += nw) {
+    const int h = u / G, g = u % G;
+    const int np = a.head_pcnt[h];
+    const int64_t base = a.head_poff[h];
+    const int kind = a.head_kind[h];
+    float acc[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) acc[i] = 0.f;
+    float M = neg_inf(), L = 0.f;
+    if (np > 0) {
+      // (m, l) of the first 32 partials stay in registers; longer lists
+      // take a second pass for the maximum
+      float m0 = neg_inf(), l0 = 0.f;
+      if (lane < np) {
+        m0 = __ldcg(&a.part_ml[((base + lane) * G + g) * 2]);
+        l0 = __ldcg(&a.part_ml[((base + lane) * G + g) * 2 + 1]);
+      }
+      M = m0;
+      for (int t = lane + 32; t < np; t += 32)
+        M = fmaxf(M, __ldcg(&a.part_ml[((base + t) * G + g) * 2]));
+      M = warp_max(M);
+      for (int t0 = 0; t0 < np; t0 += 32) {
+        float w = 0.f;
+        const int t = t0 + lane;
+        if (t < np) {
+          const float mt = t0 == 0 ? m0 : __ldcg(&a.part_ml[((base + t) * G + g) * 2]);
+          const float lt = t0 == 0 ? l0 : __ldcg(&a.part_ml[((base + t) * G + g) * 2 + 1]);
+          w = (mt == neg_inf()) ? 0.f : expf(mt - M);
+          L += lt * w;
+        }
+        const int cnt = min(32, np - t0);
+#pragma unroll 4
+        for (int v = 0; v < cnt; ++v) {
+          const float wv = __shfl_sync(0xffffffffu, w, v);
+          float ov[PL];
+          load_vec_cg<PL>(a.part_o + ((base + t0 + v) * G + g) * D + lane * PL, ov);
+#pragma unroll
+          for (int i = 0; i < PL; ++i) acc[i] += wv * ov[i];
+        }
+      }
+      L = warp_sum(L);
+    }
+    finish_row<D>(a, a.h_base + h, kind, g, M, L, acc);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct Plan {
   int nc, stages, meta_cap, smem;
-  int off_flush, off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_poff, off_misc;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // Shared-memory plan for a launch of n_heads heads: the consumer count and
-// per-consumer ring depth that keep the most pages in flight.
-bool make_plan(int D, int G, int n_heads, int max_nc, Plan* best) {
+// per-consumer ring depth that keep the most pages in flight (ties go to more
+// consumers).
+bool make_plan(int D, int n_heads, int max_nc, Plan* best) {
   const size_t stage = (size_t)2 * (D / 64) * kBS * 128;
-  const size_t fs = (size_t)D + 4;  // flush_stride<D>()
   bool found = false;
   int best_score = 0;
   for (int nc = max_nc; nc >= 2; --nc) {
     Plan p;
-    const size_t flush = (size_t)2 * nc * G * (fs + 2) * 4;
     const int meta_cap = kMetaPerConsumer * nc;
-    const size_t tail = up(flush, 16) + up((size_t)meta_cap * 8, 16) +
-                        up((size_t)nc * kMaxStages * 4, 16) + up((size_t)(n_heads + 1) * 4, 16) +
-                        up((size_t)n_heads * 4, 16) + up((size_t)n_heads, 16) +
-                        up((size_t)n_heads * 4, 16) + kMiscWords * 4;
+    const size_t tail = up((size_t)meta_cap * 8, 16) + up((size_t)nc * kMaxStages * 4, 16) +
+                        up((size_t)(n_heads + 1) * 4, 16) + up((size_t)n_heads * 4, 16) +
+                        up((size_t)n_heads, 16) + 2 * up((size_t)n_heads * 4, 16) +
+                        kMiscWords * 4;
     const size_t avail = (size_t)kSmemCap - 1024;  // alignment slack of the dynamic base
     if (avail <= tail) continue;
     int stages = (int)((avail - tail) / (stage * nc));
     if (stages > kMaxStages) stages = kMaxStages;
     if (stages < 2) continue;
     size_t off = (size_t)nc * stages * stage;
-    p.off_flush = (int)off; off += up(flush, 16);
     p.off_meta = (int)off; off += up((size_t)meta_cap * 8, 16);
     p.off_snt = (int)off; off += up((size_t)nc * stages * 4, 16);
     p.off_pref = (int)off; off += up((size_t)(n_heads + 1) * 4, 16);
     p.off_ctx = (int)off; off += up((size_t)n_heads * 4, 16);
     p.off_kind = (int)off; off += up((size_t)n_heads, 16);
     p.off_span = (int)off; off += up((size_t)n_heads * 4, 16);
+    p.off_poff = (int)off; off += up((size_t)n_heads * 4, 16);
     p.off_misc = (int)off; off += kMiscWords * 4;
     if (off + 1024 > (size_t)kSmemCap) continue;
     p.nc = nc;
@@ -990,17 +949,17 @@ bool make_plan(int D, int G, int n_heads, int max_nc, Plan* best) {
 template <typename T, int D, int GR>
 cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
   Plan pl;
-  if (!make_plan(D, a.G, a.n_heads, max_consumers<D, GR>(), &pl)) return cudaErrorInvalidValue;
+  if (!make_plan(D, a.n_heads, max_consumers<D, GR>(), &pl)) return cudaErrorInvalidValue;
   a.nc = pl.nc;
   a.stages = pl.stages;
   a.meta_cap = pl.meta_cap;
-  a.off_flush = pl.off_flush;
   a.off_meta = pl.off_meta;
   a.off_snt = pl.off_snt;
   a.off_pref = pl.off_pref;
   a.off_ctx = pl.off_ctx;
   a.off_kind = pl.off_kind;
   a.off_span = pl.off_span;
+  a.off_poff = pl.off_poff;
   a.off_misc = pl.off_misc;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -1013,8 +972,15 @@ cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  return launch_k(stream_attend_kernel<T, D, GR>, dim3(num_sms()), dim3((pl.nc + 2) * 32),
-                  (size_t)pl.smem, s, pdl, a);
+  e = launch_k(stream_attend_kernel<T, D, GR>, dim3(num_sms()), dim3((pl.nc + 1) * 32),
+               (size_t)pl.smem, s, pdl, a);
+  if (e != cudaSuccess) return e;
+  // the combine kernel always follows its attention grid with PDL: it waits
+  // for that grid's completion before reading the partials
+  const int rows = a.n_heads * a.G;
+  int grid = (rows + 7) / 8;
+  if (grid > num_sms() * 16) grid = num_sms() * 16;
+  return launch_k(stream_combine_kernel<D>, dim3(grid), dim3(256), 0, s, true, a);
 }
 
 template <typename T>
@@ -1028,12 +994,42 @@ cudaError_t dispatch(StreamArgs& a, int d, cudaStream_t s, bool pdl) {
   return cudaErrorInvalidValue;
 }
 
-int chunk_heads(const QView& q, int max_sel) {
-  // keep the stream length of one launch within int32
+// Heads per launch: the shared-memory head table holds up to kMaxChunkHeads,
+// the stream length of one launch stays within int32, and the partial scratch
+// of one launch stays within kMaxPartialBytes.
+constexpr size_t kMaxPartialBytes = (size_t)64 << 20;
+
+size_t partial_bytes_per_slot(int G, int D) { return (size_t)G * (D + 2) * 4; }
+
+int chunk_heads(const QView& q, const KvView& kv, int max_sel) {
   const long long per = (long long)(q.W > max_sel ? q.W : max_sel) + 1;
   long long ch = (long long)INT_MAX / per;
   if (ch > kMaxChunkHeads) ch = kMaxChunkHeads;
+  const int G = q.hq / kv.hkv;
+  const long long slots_cap =
+      (long long)(kMaxPartialBytes / partial_bytes_per_slot(G, kv.d)) /
+          max_consumers_rt(kv.d, G) - num_sms();
+  if (ch > slots_cap) ch = slots_cap;
   return ch < 1 ? 1 : (int)ch;
+}
+
+// Partial scratch for launches of `chunk` heads: every (head, CTA) pair of a
+// launch is at most chunk + gridDim.x - 1, times the consumer count.
+struct PartialLayout {
+  size_t o, ml, poff, pcnt, kind, total;
+};
+PartialLayout partial_layout(const QView& q, const KvView& kv, int chunk) {
+  const int G = q.hq / kv.hkv;
+  const size_t slots = (size_t)(chunk + num_sms()) * max_consumers_rt(kv.d, G);
+  PartialLayout L;
+  size_t off = 0;
+  L.o = off; off += up(slots * G * kv.d * 4, 256);
+  L.ml = off; off += up(slots * G * 2 * 4, 256);
+  L.poff = off; off += up((size_t)chunk * 4, 256);
+  L.pcnt = off; off += up((size_t)chunk * 4, 256);
+  L.kind = off; off += up((size_t)chunk, 256);
+  L.total = off;
+  return L;
 }
 
 }  // namespace
@@ -1047,10 +1043,11 @@ bool stream_attend_eligible(const QView& q, const KvView& kv) {
          (reinterpret_cast<uintptr_t>(kv.v) % 16 == 0);
 }
 
-size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv) {
-  const size_t G = (size_t)(q.hq / kv.hkv);
-  const size_t slots = (size_t)2 * num_sms();
-  return up(slots * G * kv.d * 4, 256) + up(slots * G * 2 * 4, 256);
+size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel) {
+  const int heads = q.B * kv.hkv;
+  int chunk = chunk_heads(q, kv, max_sel);
+  if (chunk > heads) chunk = heads < 1 ? 1 : heads;
+  return partial_layout(q, kv, chunk).total;
 }
 
 cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendParams& p,
@@ -1106,15 +1103,17 @@ cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendP
   a.cov0 = p.cov0;
   a.acc1 = p.acc1;
   a.cov1 = p.cov1;
-  a.head_done = p.head_done;
   a.scale = 1.0f / sqrtf((float)kv.d);
-  const size_t need = stream_attend_workspace_bytes(q, kv);
-  if (p.partial_bytes < need) return cudaErrorInvalidValue;
-  const size_t slots = (size_t)2 * num_sms();
-  a.part_o = reinterpret_cast<float*>(p.partials);
-  a.part_ml = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(p.partials) +
-                                       up(slots * a.G * kv.d * 4, 256));
-  const int chunk = chunk_heads(q, p.dense ? 1 : max_sel);
+  int chunk = chunk_heads(q, kv, p.dense ? 1 : max_sel);
+  if (chunk > heads) chunk = heads;
+  const PartialLayout L = partial_layout(q, kv, chunk);
+  if (p.partial_bytes < L.total) return cudaErrorInvalidValue;
+  uint8_t* base = reinterpret_cast<uint8_t*>(p.partials);
+  a.part_o = reinterpret_cast<float*>(base + L.o);
+  a.part_ml = reinterpret_cast<float*>(base + L.ml);
+  a.head_poff = reinterpret_cast<int32_t*>(base + L.poff);
+  a.head_pcnt = reinterpret_cast<int32_t*>(base + L.pcnt);
+  a.head_kind = base + L.kind;
   for (int h0 = 0; h0 < heads; h0 += chunk) {
     a.h_base = h0;
     a.n_heads = heads - h0 < chunk ? heads - h0 : chunk;

@@ -149,9 +149,9 @@ cudaError_t launch_attend(const QView& q, const KvView& kv, const AttendParams& 
 bool attend_supported(const QView& q, const KvView& kv);
 int attend_complement_chunk();  // logical pages per complement item
 
-// ---- attend_stream.cu (bf16 / f16, TMA-able pools; launch_attend routes) ----
+// ---- attend_stream.cu (bf16 / f16, 16-byte-aligned pools; launch_attend routes) ----
 bool stream_attend_eligible(const QView& q, const KvView& kv);
-size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv);
+size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv, int max_sel);
 cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendParams& p,
                                  int max_sel, cudaStream_t s, bool pdl);
 
