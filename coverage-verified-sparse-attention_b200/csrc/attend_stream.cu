@@ -36,11 +36,12 @@
 // one small TMA box per 64 columns would bound each SM by its TMA issue rate.
 // At the end of each head a consumer writes its state (o, m, l per query
 // row, rescaled to the exact row max) to a global partial; consumer warps
-// issue no memory fences, which would wait for their copies in flight. A
-// combine kernel, launched behind with programmatic dependent launch, merges
-// each head's partials (from every consumer of every CTA that worked on it,
-// in CTA then warp order, so results are deterministic for a given device)
-// and writes the outputs.
+// issue no memory fences while copies are in flight (a fence would wait for
+// them). When its streaming is done, a CTA merges the partials of the heads
+// that lie inside its range (one warp per query row); a head split over CTAs
+// is merged by the last of them to finish (ticket per head, no spin).
+// Partials merge in CTA then warp order, so results are deterministic for a
+// given device.
 #include <climits>
 
 #include "cvsa_common.cuh"
@@ -103,13 +104,11 @@ struct StreamArgs {
   const float* cov1;
   float* part_o;       // [slots][G][D] consumer partials of this launch
   float* part_ml;      // [slots][G][2]
-  int32_t* head_poff;  // [n_heads] first partial slot of each head (written by CTA 0)
-  int32_t* head_pcnt;  // [n_heads] partials of each head
-  uint8_t* head_kind;  // [n_heads]
+  int32_t* head_done;  // per (b, kv head) of the whole call, zero at rest
   int h_base, n_heads; // heads [h_base, h_base + n_heads) of this launch
   int nc, stages, meta_cap;
   // shared-memory carve-up, byte offsets from the 1024-aligned base
-  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_poff, off_misc;
+  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
   float scale;
 };
 
@@ -118,6 +117,7 @@ constexpr int kMiscFail = 4;       // a bounded wait gave up: stop
 constexpr int kMiscProd = 5;       // page descriptors published (local positions)
 constexpr int kMiscScan = 8;       // [33] block-scan scratch
 constexpr int kMiscCons = 48;      // [kMaxConsumers] next position each consumer reads
+constexpr int kMiscWon = 56;       // [2] this CTA merges its first / last head
 constexpr int kMiscWords = 64;
 
 // Consumer warps a launch may use: 8, or 4 where the wider per-lane state
@@ -313,12 +313,81 @@ __device__ __forceinline__ void finish_row(const StreamArgs& a, int bh, int kind
   store_row<PL>(a.out, a.out_dtype, d0, r);
 }
 
+// Partial slot of consumer k of CTA c for head h. A CTA's heads are a
+// contiguous range and CTA c's range never starts before CTA c - 1's ends, so
+// (h + c) is distinct over the (head, CTA) pairs that meet: slots stay below
+// (heads + CTAs) * NC.
+__device__ __forceinline__ int64_t partial_slot(int h, int c, int k, int nc) {
+  return (int64_t)(h + c) * nc + k;
+}
+
+// Merge query row g of head h from the partials of consumers 0..nc-1 of CTAs
+// fc..lc, in that order (deterministic), and write its outputs: the
+// split-decode reduction of cvsa/kernels/sparse_decode.py:577-606 (maximum
+// over the partials, weights exp(m_i - M), sums) at warp scale. Lane t holds
+// partial t's (m, l) (one load round for up to 32 partials); the columns of
+// kU partials are in flight together.
+template <int D>
+__device__ void merge_row(const StreamArgs& a, int h, int g, int fc, int lc, int nc, int kind) {
+  constexpr int PL = D / 32;
+  constexpr int kU = PL >= 8 ? 4 : 32 / PL;
+  const int lane = threadIdx.x & 31;
+  const int G = a.G;
+  const int np = (lc - fc + 1) * nc;
+  auto row_of = [&](int t) -> int64_t { return partial_slot(h, fc + t / nc, t % nc, nc) * G + g; };
+  float m0 = neg_inf(), l0 = 0.f;
+  if (lane < np) {
+    m0 = __ldcg(&a.part_ml[row_of(lane) * 2]);
+    l0 = __ldcg(&a.part_ml[row_of(lane) * 2 + 1]);
+  }
+  float M = m0;
+  for (int t = lane + 32; t < np; t += 32) M = fmaxf(M, __ldcg(&a.part_ml[row_of(t) * 2]));
+  M = warp_max(M);
+  float L = 0.f, acc[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) acc[i] = 0.f;
+  if (M != neg_inf()) {
+    for (int t0 = 0; t0 < np; t0 += 32) {
+      float w = 0.f;
+      const int t = t0 + lane;
+      if (t < np) {
+        const float mt = t0 == 0 ? m0 : __ldcg(&a.part_ml[row_of(t) * 2]);
+        const float lt = t0 == 0 ? l0 : __ldcg(&a.part_ml[row_of(t) * 2 + 1]);
+        w = (mt == neg_inf()) ? 0.f : expf(mt - M);
+        L += lt * w;
+      }
+      const int cnt = min(32, np - t0);
+      for (int v0 = 0; v0 < cnt; v0 += kU) {
+        float ov[kU][PL];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          if (v0 + u < cnt) {
+            load_vec_cg<PL>(a.part_o + row_of(t0 + v0 + u) * D + lane * PL, ov[u]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < PL; ++i) ov[u][i] = 0.f;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const float wv = __shfl_sync(0xffffffffu, w, (v0 + u) & 31);
+#pragma unroll
+          for (int i = 0; i < PL; ++i) acc[i] += wv * ov[u][i];
+        }
+      }
+    }
+    L = warp_sum(L);
+  }
+  finish_row<D>(a, a.h_base + h, kind, g, M, L, acc);
+}
+
 template <typename T, int D, int GR>
 __global__ void __launch_bounds__((max_consumers<D, GR>() + 1) * 32, 1)
 stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   constexpr int kSub = D / 64;                         // 64-column slices
   constexpr int kTile = kBS * 128;                     // one swizzled slice of a page
   constexpr uint32_t kStageBytes = 2 * kSub * kTile;   // K and V of one page
+  constexpr int PL = D / 32;                           // output columns per lane
   constexpr int kRowChunks = D / 8;                    // 16-byte chunks per token row
   constexpr int kCopies = kBS * kRowChunks / 32;       // cp.async per lane per tensor and page
 
@@ -331,7 +400,6 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   int* ctxv = reinterpret_cast<int*>(sm + a.off_ctx);
   uint8_t* kindv = sm + a.off_kind;
   uint32_t* span = reinterpret_cast<uint32_t*>(sm + a.off_span);  // first CTA << 16 | last CTA
-  int* poff = reinterpret_cast<int*>(sm + a.off_poff);  // first partial slot of each head
   int* misc = reinterpret_cast<int*>(sm + a.off_misc);
   volatile int* vmisc = misc;
 
@@ -446,34 +514,25 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   __syncthreads();
   auto first_cta = [&](int h) -> int { return (int)(span[h] >> 16); };
   auto last_cta = [&](int h) -> int { return (int)(span[h] & 0xffffu); };
-  // partial slots: every consumer of every CTA that works on a non-empty head
-  // writes one, at poff[h] + (c - first CTA) * NC + consumer
-  {
-    const int per = (H + nthreads - 1) / nthreads;
-    const int h0 = min(tid * per, H), h1 = min(h0 + per, H);
-    int sum = 0;
-    for (int h = h0; h < h1; ++h) {
-      const int n = pref[h + 1] > pref[h] ? (last_cta(h) - first_cta(h) + 1) * NC : 0;
-      poff[h] = n;
-      sum += n;
-    }
-    int total = 0;
-    int base = block_excl_scan(sum, misc + kMiscScan, &total);
-    for (int h = h0; h < h1; ++h) {
-      const int n = poff[h];
-      poff[h] = base;
-      if (c == 0) {
-        a.head_poff[h] = base;
-        a.head_pcnt[h] = n;
-        a.head_kind[h] = kindv[h];
-      }
-      base += n;
-    }
-  }
-  __syncthreads();
-  // let the combine kernel's CTAs be scheduled as this grid drains
+  auto empty_head = [&](int h) -> bool { return pref[h + 1] == pref[h]; };
+  // let the next kernel's CTAs be scheduled as this grid drains (it waits for
+  // this grid's completion before reading anything it wrote)
   pdl_launch_dependents();
+
+  // Empty heads (no pages) are finished from the empty state by CTA h % C,
+  // one warp per query row.
+  auto finish_empty_heads = [&]() {
+    float z[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) z[i] = 0.f;
+    const int mine = c < H ? (H - 1 - c) / C + 1 : 0;
+    for (int u = warp; u < mine * G; u += nthreads / 32) {
+      const int h = c + (u / G) * C, g = u % G;
+      if (empty_head(h)) finish_row<D>(a, a.h_base + h, kindv[h], g, neg_inf(), 0.f, z);
+    }
+  };
   if (P == 0) {
+    finish_empty_heads();
     if (warp == NC) commit_heads();
     return;
   }
@@ -551,8 +610,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
       if (vmisc[kMiscFail]) break;
     }
     commit_heads();
-    return;
-  }
+  } else {
 
   // =============================== consumers ===============================
   const int k = warp;
@@ -657,10 +715,10 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
 
   // Write the state of head h as this consumer's partial, rescaled from the
   // reference max m_use to the exact row max (f <= 1). Empty heads have no
-  // partials (the combine kernel finishes them from the empty state).
+  // partials.
   auto flush_head = [&](int h) {
-    if (pref[h + 1] == pref[h]) return;
-    const int64_t slot = poff[h] + (c - first_cta(h)) * NC + k;
+    if (empty_head(h)) return;
+    const int64_t slot = partial_slot(h, c, k, NC);
 #pragma unroll
     for (int n = 0; n < GR; ++n)
 #pragma unroll
@@ -827,70 +885,55 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     flush_head(h);
     reset_state();
   }
-  // no copy may still be landing in shared memory when the warp exits
+  // no copy may still be landing in shared memory past this point; with none
+  // in flight, a fence is cheap: it makes this warp's partials visible to the
+  // CTA that merges a split head before this CTA takes its ticket
   asm volatile("cp.async.wait_all;" ::: "memory");
-}
+  __threadfence();
+  }  // consumers
 
-// ---------------------------------------------------------------------------
-// combine: one warp per (head, query row)
-// ---------------------------------------------------------------------------
-// Merges the head's consumer partials in slot order (CTA, then consumer) and
-// writes the outputs; a head without partials is finished from the empty
-// state. Restates the split-decode reduction of
-// cvsa/kernels/sparse_decode.py:577-606 (max over partials, weights
-// exp(m_i - M), sums) at warp scale.
-template <int D>
-__global__ void __launch_bounds__(256) stream_combine_kernel(const __grid_constant__ StreamArgs a) {
-  constexpr int PL = D / 32;
-  pdl_wait();
-  const int lane = threadIdx.x & 31;
-  const int wg = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nw = (gridDim.x * blockDim.x) >> 5;
-  const int G = a.G;
-  for (int u = wg; u < a.n_heads * G; u += nw) {
-    const int h = u / G, g = u % G;
-    const int np = a.head_pcnt[h];
-    const int64_t base = a.head_poff[h];
-    const int kind = a.head_kind[h];
-    float acc[PL];
-#pragma unroll
-    for (int i = 0; i < PL; ++i) acc[i] = 0.f;
-    float M = neg_inf(), L = 0.f;
-    if (np > 0) {
-      // (m, l) of the first 32 partials stay in registers; longer lists
-      // take a second pass for the maximum
-      float m0 = neg_inf(), l0 = 0.f;
-      if (lane < np) {
-        m0 = __ldcg(&a.part_ml[((base + lane) * G + g) * 2]);
-        l0 = __ldcg(&a.part_ml[((base + lane) * G + g) * 2 + 1]);
-      }
-      M = m0;
-      for (int t = lane + 32; t < np; t += 32)
-        M = fmaxf(M, __ldcg(&a.part_ml[((base + t) * G + g) * 2]));
-      M = warp_max(M);
-      for (int t0 = 0; t0 < np; t0 += 32) {
-        float w = 0.f;
-        const int t = t0 + lane;
-        if (t < np) {
-          const float mt = t0 == 0 ? m0 : __ldcg(&a.part_ml[((base + t) * G + g) * 2]);
-          const float lt = t0 == 0 ? l0 : __ldcg(&a.part_ml[((base + t) * G + g) * 2 + 1]);
-          w = (mt == neg_inf()) ? 0.f : expf(mt - M);
-          L += lt * w;
-        }
-        const int cnt = min(32, np - t0);
-#pragma unroll 4
-        for (int v = 0; v < cnt; ++v) {
-          const float wv = __shfl_sync(0xffffffffu, w, v);
-          float ov[PL];
-          load_vec_cg<PL>(a.part_o + ((base + t0 + v) * G + g) * D + lane * PL, ov);
-#pragma unroll
-          for (int i = 0; i < PL; ++i) acc[i] += wv * ov[i];
+  // ============================ finish the heads ============================
+  // Every warp is done streaming (no copies in flight): the partials written
+  // by this CTA's consumers are visible to the whole CTA after the barrier.
+  __syncthreads();
+  if (vmisc[kMiscFail]) return;  // a copy never arrived: leave the outputs alone
+  // Merges, one warp per query row. This CTA's split heads can only be its
+  // first and its last head; a split head is merged by the last of its CTAs
+  // to get here (ticket per head, no spin): the producer warp takes the
+  // tickets while the consumer warps merge the rows of the heads inside this
+  // CTA's range, then every warp takes the rows of the split heads won.
+  int* won = misc + kMiscWon;
+  if (warp == NC) {
+    if (lane == 0) {
+      for (int i = 0; i < 2; ++i) {
+        const int h = i == 0 ? hlo : hhi;
+        won[i] = 0;
+        if (hlo > hhi || (i == 1 && hhi == hlo) || empty_head(h) ||
+            first_cta(h) == last_cta(h))
+          continue;  // no heads, or not split
+        __threadfence();
+        const int t = atomicAdd(&a.head_done[a.h_base + h], 1);
+        if (t == last_cta(h) - first_cta(h)) {
+          won[i] = 1;
+          a.head_done[a.h_base + h] = 0;
+          __threadfence();
         }
       }
-      L = warp_sum(L);
     }
-    finish_row<D>(a, a.h_base + h, kind, g, M, L, acc);
+  } else {
+    for (int u = warp; u < (hhi - hlo + 1) * G; u += NC) {
+      const int h = hlo + u / G, g = u % G;
+      if (!empty_head(h) && first_cta(h) == last_cta(h)) merge_row<D>(a, h, g, c, c, NC, kindv[h]);
+    }
   }
+  __syncthreads();
+  for (int u = warp; u < 2 * G; u += nthreads / 32) {
+    const int i = u / G, g = u % G;
+    if (!won[i]) continue;
+    const int h = i == 0 ? hlo : hhi;
+    merge_row<D>(a, h, g, first_cta(h), last_cta(h), NC, kindv[h]);
+  }
+  finish_empty_heads();
 }
 
 // ---------------------------------------------------------------------------
@@ -898,7 +941,7 @@ __global__ void __launch_bounds__(256) stream_combine_kernel(const __grid_consta
 // ---------------------------------------------------------------------------
 struct Plan {
   int nc, stages, meta_cap, smem;
-  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_poff, off_misc;
+  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -915,8 +958,7 @@ bool make_plan(int D, int n_heads, int max_nc, Plan* best) {
     const int meta_cap = kMetaPerConsumer * nc;
     const size_t tail = up((size_t)meta_cap * 8, 16) + up((size_t)nc * kMaxStages * 4, 16) +
                         up((size_t)(n_heads + 1) * 4, 16) + up((size_t)n_heads * 4, 16) +
-                        up((size_t)n_heads, 16) + 2 * up((size_t)n_heads * 4, 16) +
-                        kMiscWords * 4;
+                        up((size_t)n_heads, 16) + up((size_t)n_heads * 4, 16) + kMiscWords * 4;
     const size_t avail = (size_t)kSmemCap - 1024;  // alignment slack of the dynamic base
     if (avail <= tail) continue;
     int stages = (int)((avail - tail) / (stage * nc));
@@ -929,14 +971,15 @@ bool make_plan(int D, int n_heads, int max_nc, Plan* best) {
     p.off_ctx = (int)off; off += up((size_t)n_heads * 4, 16);
     p.off_kind = (int)off; off += up((size_t)n_heads, 16);
     p.off_span = (int)off; off += up((size_t)n_heads * 4, 16);
-    p.off_poff = (int)off; off += up((size_t)n_heads * 4, 16);
     p.off_misc = (int)off; off += kMiscWords * 4;
     if (off + 1024 > (size_t)kSmemCap) continue;
     p.nc = nc;
     p.stages = stages;
     p.meta_cap = meta_cap;
     p.smem = (int)(off + 1024);
-    const int score = nc * stages;
+    // three stages keep two pages in flight per consumer while it computes
+    // one; past that, more consumers beat deeper rings
+    const int score = nc * (stages < 3 ? stages : 3) * 16 + nc * stages;
     if (!found || score > best_score) {
       *best = p;
       best_score = score;
@@ -959,7 +1002,6 @@ cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
   a.off_ctx = pl.off_ctx;
   a.off_kind = pl.off_kind;
   a.off_span = pl.off_span;
-  a.off_poff = pl.off_poff;
   a.off_misc = pl.off_misc;
   static bool attr_set[64] = {};
   int dev = 0;
@@ -972,15 +1014,8 @@ cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  e = launch_k(stream_attend_kernel<T, D, GR>, dim3(num_sms()), dim3((pl.nc + 1) * 32),
-               (size_t)pl.smem, s, pdl, a);
-  if (e != cudaSuccess) return e;
-  // the combine kernel always follows its attention grid with PDL: it waits
-  // for that grid's completion before reading the partials
-  const int rows = a.n_heads * a.G;
-  int grid = (rows + 7) / 8;
-  if (grid > num_sms() * 16) grid = num_sms() * 16;
-  return launch_k(stream_combine_kernel<D>, dim3(grid), dim3(256), 0, s, true, a);
+  return launch_k(stream_attend_kernel<T, D, GR>, dim3(num_sms()), dim3((pl.nc + 1) * 32),
+                  (size_t)pl.smem, s, pdl, a);
 }
 
 template <typename T>
@@ -1016,7 +1051,7 @@ int chunk_heads(const QView& q, const KvView& kv, int max_sel) {
 // Partial scratch for launches of `chunk` heads: every (head, CTA) pair of a
 // launch is at most chunk + gridDim.x - 1, times the consumer count.
 struct PartialLayout {
-  size_t o, ml, poff, pcnt, kind, total;
+  size_t o, ml, total;
 };
 PartialLayout partial_layout(const QView& q, const KvView& kv, int chunk) {
   const int G = q.hq / kv.hkv;
@@ -1025,9 +1060,6 @@ PartialLayout partial_layout(const QView& q, const KvView& kv, int chunk) {
   size_t off = 0;
   L.o = off; off += up(slots * G * kv.d * 4, 256);
   L.ml = off; off += up(slots * G * 2 * 4, 256);
-  L.poff = off; off += up((size_t)chunk * 4, 256);
-  L.pcnt = off; off += up((size_t)chunk * 4, 256);
-  L.kind = off; off += up((size_t)chunk, 256);
   L.total = off;
   return L;
 }
@@ -1111,9 +1143,7 @@ cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendP
   uint8_t* base = reinterpret_cast<uint8_t*>(p.partials);
   a.part_o = reinterpret_cast<float*>(base + L.o);
   a.part_ml = reinterpret_cast<float*>(base + L.ml);
-  a.head_poff = reinterpret_cast<int32_t*>(base + L.poff);
-  a.head_pcnt = reinterpret_cast<int32_t*>(base + L.pcnt);
-  a.head_kind = base + L.kind;
+  a.head_done = p.head_done;
   for (int h0 = 0; h0 < heads; h0 += chunk) {
     a.h_base = h0;
     a.n_heads = heads - h0 < chunk ? heads - h0 : chunk;
