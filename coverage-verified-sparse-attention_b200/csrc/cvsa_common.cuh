@@ -228,6 +228,18 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
   }
 }
 
+// Bulk (untiled) global -> shared copy of `bytes` (multiple of 16, both
+// addresses 16-byte aligned) completing on `bar` with complete_tx; no
+// multicast. `policy` is an L2 cache policy (make_evict_first_policy).
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
