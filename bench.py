@@ -246,6 +246,71 @@ def build_layers(dev, layers):
     return wls
 
 
+C3_LAYERS = 16
+
+
+def measure_config3(dev, steps, warmup, ws):
+    """Config 3 (single 128K sequence, Llama-8B geometry, 5 % budget): the same
+    graph-captured lazy M=4 schedule over C3_LAYERS independent layers (537 MB of
+    K+V each). Returns the achieved GB/s on algorithmic KV bytes and us/layer."""
+    from cvsa import _lib, synthetic
+    from cvsa.backend import CVSABackend
+
+    wls = [synthetic.config3(device=dev, seed=3000 + l, gen_device=str(dev))
+           for l in range(C3_LAYERS)]
+    torch.cuda.synchronize()
+    B, Hq, D = wls[0].q.shape
+    hkv = wls[0].num_kv_heads
+    scoring = sum(_scoring_pages(wl.context_lens, hkv) * KP_BYTES for wl in wls)
+    be = CVSABackend(hkv, Hq, D, 16, num_layers=C3_LAYERS, budget_pct=0.05,
+                     coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
+                     sink_pages=1, local_pages=2)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs = {}
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            for l, wl in enumerate(wls):
+                be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+                be.step_done(l, C3_LAYERS)
+        side.synchronize()
+        for kind, step_idx in (("lazy", 0), ("reuse", 1)):
+            g = torch.cuda.CUDAGraph()
+            be._step = step_idx
+            with torch.cuda.graph(g, stream=side):
+                for l, wl in enumerate(wls):
+                    be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+            graphs[kind] = g
+    torch.cuda.current_stream(dev).wait_stream(side)
+    for s in range(M_INTERVAL):
+        graphs["lazy" if s % M_INTERVAL == 0 else "reuse"].replay()
+    torch.cuda.synchronize()
+    lazy_steps = sum(1 for s in range(steps) if s % M_INTERVAL == 0)
+    _barrier(ws)
+    torch.cuda.synchronize()
+    c0 = be._counter_values()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        graphs["lazy" if s % M_INTERVAL == 0 else "reuse"].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    ms = _max_over_ranks(e0.elapsed_time(e1), ws)
+    c1 = be._counter_values()
+    pages = c1[_lib.CTR_PAGES_ATTENDED] - c0[_lib.CTR_PAGES_ATTENDED]
+    nbytes = _sum_over_ranks(float(pages * 2 * KP_BYTES + lazy_steps * scoring), ws)
+    stats = be.get_stats()
+    del graphs
+    return {"workload": "config3: B=1, Hq=32, Hkv=8, D=128, bf16, ctx=131072 (8192 pages), "
+                        f"budget 5% (409) + sink 1 + local 2, tau=0.9, lazy M=4, {C3_LAYERS} "
+                        "layers with independent pools (537 MB K+V each)",
+            "value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s",
+            "us_per_layer": ms * 1e3 / (steps * C3_LAYERS), "steps": steps,
+            "per_head_accept_rate": stats.get("per_head_accept_rate")}
+
+
 def run_cvsa(args, ws, rank, local):
     import ctypes
 
@@ -415,6 +480,12 @@ def run_cvsa(args, ws, rank, local):
     h2d = sum(h.numel() * h.element_size() for h in q_host)
     del graphs
 
+    # ---- config 3 (128K single sequence): the metric's second context ----
+    c3 = None
+    if not args.no_c3:
+        c3 = measure_config3(dev, args.steps, warm, ws)
+        c3["frac_of_peak"] = c3["value"] / (_peaks()[0] * ws)
+
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -444,7 +515,7 @@ def run_cvsa(args, ws, rank, local):
             "us_per_layer": us_per_layer,
             "eager_us_per_layer": ms_eager * 1e3 / (args.steps * layers),
             "tokens_per_s": B * ws * args.steps / (ms_max * 1e-3),
-            "roofline": {"bound": "hbm", "kernel": "score_pages_kernel",
+            "roofline": {"bound": "hbm", "kernel": "score_stream_kernel",
                          "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": (achieved / peak) if achieved else None,
                          "traffic": traffic, "peak_kind": peak_kind,
@@ -467,6 +538,8 @@ def run_cvsa(args, ws, rank, local):
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if c3 is not None:
+            line["config3_128k"] = c3
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -480,6 +553,7 @@ def main():
     ap.add_argument("--impl", default="cvsa", choices=["cvsa", "reference"])
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-c3", action="store_true", help="skip the config-3 (128K) measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -523,7 +523,9 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   sp.step_flags = io->step_flags;
   int32_t* comp_cnt = reinterpret_cast<int32_t*>(ws + L.comp_cnt);
   int32_t* comp_off = reinterpret_cast<int32_t*>(ws + L.comp_off);
-  if (recover) {
+  // the compact complement-item list only serves the general-layout kernel
+  const bool comp_items = recover && !stream_attend_eligible(q, kv);
+  if (comp_items) {
     sp.comp_cnt = comp_cnt;
     sp.comp_off = comp_off;
     sp.comp_chunk = attend_complement_chunk();
@@ -541,7 +543,7 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   ap.src_select = (mode == CVSA_MODE_LAZY) ? 2 : 1;
   ap.decision = sync + 2;
   ap.recover = recover;
-  ap.comp_off = recover ? comp_off : nullptr;
+  ap.comp_off = comp_items ? comp_off : nullptr;
   ap.accept = acc_new;
   ap.bitmap = bitmap;
   ap.bitmap_words = bitmap_words(q.W);

@@ -104,6 +104,8 @@ struct StreamArgs {
   const float* cov1;
   float* part_o;       // [slots][G][D] consumer partials of this launch
   float* part_ml;      // [slots][G][2]
+  float* cpart_o;      // [heads + CTAs][G][D] per-CTA partials of split heads
+  float* cpart_ml;     // [heads + CTAs][G][2]
   int32_t* head_done;  // per (b, kv head) of the whole call, zero at rest
   int h_base, n_heads; // heads [h_base, h_base + n_heads) of this launch
   int nc, stages, meta_cap;
@@ -321,64 +323,60 @@ __device__ __forceinline__ int64_t partial_slot(int h, int c, int k, int nc) {
   return (int64_t)(h + c) * nc + k;
 }
 
-// Merge query row g of head h from the partials of consumers 0..nc-1 of CTAs
-// fc..lc, in that order (deterministic), and write its outputs: the
-// split-decode reduction of cvsa/kernels/sparse_decode.py:577-606 (maximum
-// over the partials, weights exp(m_i - M), sums) at warp scale. Lane t holds
-// partial t's (m, l) (one load round for up to 32 partials); the columns of
-// kU partials are in flight together.
-template <int D>
-__device__ void merge_row(const StreamArgs& a, int h, int g, int fc, int lc, int nc, int kind) {
+// Merge np partial rows, the t-th at row index row_of(t) of (po, pml), in
+// order t = 0..np-1 (deterministic), into (M, L, acc): the split-decode
+// reduction of cvsa/kernels/sparse_decode.py:577-606 (maximum over the
+// partials, weights exp(m_t - M), sums) at warp scale. Lane t holds partial
+// t's (m, l) (one load round for up to 32 partials); the columns of kU
+// partials are in flight together.
+template <int D, class RowOf>
+__device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_of, float& M,
+                           float& L, float (&acc)[D / 32]) {
   constexpr int PL = D / 32;
   constexpr int kU = PL >= 8 ? 4 : 32 / PL;
   const int lane = threadIdx.x & 31;
-  const int G = a.G;
-  const int np = (lc - fc + 1) * nc;
-  auto row_of = [&](int t) -> int64_t { return partial_slot(h, fc + t / nc, t % nc, nc) * G + g; };
   float m0 = neg_inf(), l0 = 0.f;
   if (lane < np) {
-    m0 = __ldcg(&a.part_ml[row_of(lane) * 2]);
-    l0 = __ldcg(&a.part_ml[row_of(lane) * 2 + 1]);
+    m0 = __ldcg(&pml[row_of(lane) * 2]);
+    l0 = __ldcg(&pml[row_of(lane) * 2 + 1]);
   }
-  float M = m0;
-  for (int t = lane + 32; t < np; t += 32) M = fmaxf(M, __ldcg(&a.part_ml[row_of(t) * 2]));
+  M = m0;
+  for (int t = lane + 32; t < np; t += 32) M = fmaxf(M, __ldcg(&pml[row_of(t) * 2]));
   M = warp_max(M);
-  float L = 0.f, acc[PL];
+  L = 0.f;
 #pragma unroll
   for (int i = 0; i < PL; ++i) acc[i] = 0.f;
-  if (M != neg_inf()) {
-    for (int t0 = 0; t0 < np; t0 += 32) {
-      float w = 0.f;
-      const int t = t0 + lane;
-      if (t < np) {
-        const float mt = t0 == 0 ? m0 : __ldcg(&a.part_ml[row_of(t) * 2]);
-        const float lt = t0 == 0 ? l0 : __ldcg(&a.part_ml[row_of(t) * 2 + 1]);
-        w = (mt == neg_inf()) ? 0.f : expf(mt - M);
-        L += lt * w;
+  if (M == neg_inf()) return;
+  for (int t0 = 0; t0 < np; t0 += 32) {
+    float w = 0.f;
+    const int t = t0 + lane;
+    if (t < np) {
+      const float mt = t0 == 0 ? m0 : __ldcg(&pml[row_of(t) * 2]);
+      const float lt = t0 == 0 ? l0 : __ldcg(&pml[row_of(t) * 2 + 1]);
+      w = (mt == neg_inf()) ? 0.f : expf(mt - M);
+      L += lt * w;
+    }
+    const int cnt = min(32, np - t0);
+    for (int v0 = 0; v0 < cnt; v0 += kU) {
+      float ov[kU][PL];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        if (v0 + u < cnt) {
+          load_vec_cg<PL>(po + row_of(t0 + v0 + u) * D + lane * PL, ov[u]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < PL; ++i) ov[u][i] = 0.f;
+        }
       }
-      const int cnt = min(32, np - t0);
-      for (int v0 = 0; v0 < cnt; v0 += kU) {
-        float ov[kU][PL];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          if (v0 + u < cnt) {
-            load_vec_cg<PL>(a.part_o + row_of(t0 + v0 + u) * D + lane * PL, ov[u]);
-          } else {
+      for (int u = 0; u < kU; ++u) {
+        const float wv = __shfl_sync(0xffffffffu, w, (v0 + u) & 31);
 #pragma unroll
-            for (int i = 0; i < PL; ++i) ov[u][i] = 0.f;
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < kU; ++u) {
-          const float wv = __shfl_sync(0xffffffffu, w, (v0 + u) & 31);
-#pragma unroll
-          for (int i = 0; i < PL; ++i) acc[i] += wv * ov[u][i];
-        }
+        for (int i = 0; i < PL; ++i) acc[i] += wv * ov[u][i];
       }
     }
-    L = warp_sum(L);
   }
-  finish_row<D>(a, a.h_base + h, kind, g, M, L, acc);
+  L = warp_sum(L);
 }
 
 template <typename T, int D, int GR>
@@ -897,33 +895,53 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   // by this CTA's consumers are visible to the whole CTA after the barrier.
   __syncthreads();
   if (vmisc[kMiscFail]) return;  // a copy never arrived: leave the outputs alone
-  // Merges, one warp per query row. This CTA's split heads can only be its
-  // first and its last head; a split head is merged by the last of its CTAs
-  // to get here (ticket per head, no spin): the producer warp takes the
-  // tickets while the consumer warps merge the rows of the heads inside this
-  // CTA's range, then every warp takes the rows of the split heads won.
-  int* won = misc + kMiscWon;
-  if (warp == NC) {
-    if (lane == 0) {
-      for (int i = 0; i < 2; ++i) {
-        const int h = i == 0 ? hlo : hhi;
-        won[i] = 0;
-        if (hlo > hhi || (i == 1 && hhi == hlo) || empty_head(h) ||
-            first_cta(h) == last_cta(h))
-          continue;  // no heads, or not split
-        __threadfence();
-        const int t = atomicAdd(&a.head_done[a.h_base + h], 1);
-        if (t == last_cta(h) - first_cta(h)) {
-          won[i] = 1;
-          a.head_done[a.h_base + h] = 0;
-          __threadfence();
+  // Merges, one warp per query row. Heads inside this CTA's range are merged
+  // from its consumers' partials and finished. A head split over CTAs (only
+  // this CTA's first and last head can be) is first merged over this CTA's
+  // consumers into one CTA partial (slot head + CTA); the last of its CTAs to
+  // get here (ticket per head, no spin) merges the CTA partials in CTA order.
+  auto split_head = [&](int i) -> int {  // this CTA's first (0) / last (1) head if split
+    const int h = i == 0 ? hlo : hhi;
+    if (hlo > hhi || (i == 1 && hhi == hlo) || empty_head(h) || first_cta(h) == last_cta(h))
+      return -1;
+    return h;
+  };
+  {
+    const int nrow = (hhi - hlo + 1) * G;
+    for (int u = warp; u < nrow; u += nthreads / 32) {
+      const int h = hlo + u / G, g = u % G;
+      if (empty_head(h)) continue;
+      float M, L, acc[PL];
+      merge_rows<D>(a.part_o, a.part_ml, NC,
+                    [&](int t) -> int64_t { return partial_slot(h, c, t, NC) * G + g; }, M, L,
+                    acc);
+      if (first_cta(h) == last_cta(h)) {
+        finish_row<D>(a, a.h_base + h, kindv[h], g, M, L, acc);
+      } else {
+        const int64_t row = (int64_t)(h + c) * G + g;
+        store_vec_cg<PL>(a.cpart_o + row * D + lane * PL, acc);
+        if (lane == 0) {
+          __stcg(&a.cpart_ml[row * 2], M);
+          __stcg(&a.cpart_ml[row * 2 + 1], L);
         }
+        __threadfence();
       }
     }
-  } else {
-    for (int u = warp; u < (hhi - hlo + 1) * G; u += NC) {
-      const int h = hlo + u / G, g = u % G;
-      if (!empty_head(h) && first_cta(h) == last_cta(h)) merge_row<D>(a, h, g, c, c, NC, kindv[h]);
+  }
+  __syncthreads();
+  int* won = misc + kMiscWon;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      const int h = split_head(i);
+      won[i] = 0;
+      if (h < 0) continue;
+      __threadfence();
+      const int t = atomicAdd(&a.head_done[a.h_base + h], 1);
+      if (t == last_cta(h) - first_cta(h)) {
+        won[i] = 1;
+        a.head_done[a.h_base + h] = 0;
+        __threadfence();
+      }
     }
   }
   __syncthreads();
@@ -931,7 +949,11 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     const int i = u / G, g = u % G;
     if (!won[i]) continue;
     const int h = i == 0 ? hlo : hhi;
-    merge_row<D>(a, h, g, first_cta(h), last_cta(h), NC, kindv[h]);
+    const int fc = first_cta(h);
+    float M, L, acc[PL];
+    merge_rows<D>(a.cpart_o, a.cpart_ml, last_cta(h) - fc + 1,
+                  [&](int t) -> int64_t { return (int64_t)(h + fc + t) * G + g; }, M, L, acc);
+    finish_row<D>(a, a.h_base + h, kindv[h], g, M, L, acc);
   }
   finish_empty_heads();
 }
@@ -1051,7 +1073,7 @@ int chunk_heads(const QView& q, const KvView& kv, int max_sel) {
 // Partial scratch for launches of `chunk` heads: every (head, CTA) pair of a
 // launch is at most chunk + gridDim.x - 1, times the consumer count.
 struct PartialLayout {
-  size_t o, ml, total;
+  size_t o, ml, co, cml, total;
 };
 PartialLayout partial_layout(const QView& q, const KvView& kv, int chunk) {
   const int G = q.hq / kv.hkv;
@@ -1060,6 +1082,9 @@ PartialLayout partial_layout(const QView& q, const KvView& kv, int chunk) {
   size_t off = 0;
   L.o = off; off += up(slots * G * kv.d * 4, 256);
   L.ml = off; off += up(slots * G * 2 * 4, 256);
+  const size_t cslots = (size_t)chunk + num_sms();
+  L.co = off; off += up(cslots * G * kv.d * 4, 256);
+  L.cml = off; off += up(cslots * G * 2 * 4, 256);
   L.total = off;
   return L;
 }
@@ -1143,6 +1168,8 @@ cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendP
   uint8_t* base = reinterpret_cast<uint8_t*>(p.partials);
   a.part_o = reinterpret_cast<float*>(base + L.o);
   a.part_ml = reinterpret_cast<float*>(base + L.ml);
+  a.cpart_o = reinterpret_cast<float*>(base + L.co);
+  a.cpart_ml = reinterpret_cast<float*>(base + L.cml);
   a.head_done = p.head_done;
   for (int h0 = 0; h0 < heads; h0 += chunk) {
     a.h_base = h0;

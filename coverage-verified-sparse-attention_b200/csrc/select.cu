@@ -145,6 +145,27 @@ __device__ __forceinline__ float lse_list_warp(const float* row, int W, const in
   return m + logf(sum + 1e-30f);
 }
 
+// lse_list_warp over a shared-memory copy of the row, with the first 64
+// list entries loaded up front (one load round).
+__device__ __forceinline__ float lse_list_smem(const float* srow, int W, const int32_t* idx, int n) {
+  const int lane = threadIdx.x & 31;
+  const int pg0 = lane < n ? idx[lane] : -1;
+  const int pg1 = lane + 32 < n ? idx[lane + 32] : -1;
+  auto val = [&](int pg) -> float { return (pg >= 0 && pg < W) ? srow[pg] : neg_inf(); };
+  float m = fmaxf(val(pg0), val(pg1));
+  for (int i = lane + 64; i < n; i += 32) m = fmaxf(m, val(idx[i]));
+  m = fmaxf(warp_max(m), -1e20f);
+  float sum = 0.f;
+  if (pg0 >= 0 && pg0 < W) sum += expf(srow[pg0] - m);
+  if (pg1 >= 0 && pg1 < W) sum += expf(srow[pg1] - m);
+  for (int i = lane + 64; i < n; i += 32) {
+    const int pg = idx[i];
+    if (pg >= 0 && pg < W) sum += expf(srow[pg] - m);
+  }
+  sum = warp_sum(sum);
+  return m + logf(sum + 1e-30f);
+}
+
 __device__ __forceinline__ void count_head(const SelectParams& p, bool acc) {
   if (!p.counters) return;
   atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_ACCEPT]),
@@ -226,7 +247,32 @@ __device__ void finish_select(const SelectParams& p, int cta_rejects, int* s_fla
 // ---------------------------------------------------------------------------
 // warp per (b, h): tables of up to 32 * EPL pages
 // ---------------------------------------------------------------------------
-constexpr int kWarpSelWarps = 8;
+// k at or below which the threshold is found by k max-extraction rounds over
+// per-lane sorted keys rather than by the 32-step bisection
+constexpr int kExtractMax = 64;
+
+// Ascending bitonic sort of N (power of two) values held in registers.
+template <int N>
+__device__ __forceinline__ void sort_asc(uint32_t (&a)[N]) {
+#pragma unroll
+  for (int size = 2; size <= N; size <<= 1)
+#pragma unroll
+    for (int stride = size / 2; stride > 0; stride >>= 1)
+#pragma unroll
+      for (int i = 0; i < N; ++i) {
+        const int j = i ^ stride;
+        if (j > i) {
+          const uint32_t x = a[i], y = a[j];
+          const bool up = (i & size) == 0;
+          a[i] = up ? min(x, y) : max(x, y);
+          a[j] = up ? max(x, y) : min(x, y);
+        }
+      }
+}
+
+// Two heads per CTA: the per-head search is instruction-bound, so heads are
+// spread over as many SMs as possible.
+constexpr int kWarpSelWarps = 2;
 
 template <int EPL>
 __global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(SelectParams p) {
@@ -234,9 +280,18 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(Se
   __shared__ int wsum[NT / 32];
   __shared__ int s_flag[2];
   __shared__ int s_rej;
+  __shared__ int s_heads[2];  // heads counted / accepted by this CTA
+  __shared__ float s_row_all[kWarpSelWarps][32 * EPL];
+  if (threadIdx.x < 2) s_heads[threadIdx.x] = 0;
   if (threadIdx.x == 0) s_rej = 0;
   __syncthreads();
   pdl_wait();
+  // head counters: one atomic per CTA instead of one per head
+  auto count = [&](bool acc) {
+    if (!p.counters) return;
+    atomicAdd(&s_heads[0], 1);
+    if (acc) atomicAdd(&s_heads[1], 1);
+  };
 
   const int lane = threadIdx.x & 31;
   const int heads = p.B * p.hkv;
@@ -244,12 +299,29 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(Se
   if (bh < heads) {
     const int b = bh / p.hkv;
     const int W = p.W;
-    const int nv = min(n_valid_pages(p.lens[b], p.bs), W);
     const float* row = p.scores + (int64_t)bh * W;
     const int p0 = lane * EPL;
+    // every load of the head is issued before any is used
     float s[EPL];
+    if ((W % 4) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
 #pragma unroll
-    for (int i = 0; i < EPL; ++i) s[i] = (p0 + i < W) ? __ldg(row + p0 + i) : neg_inf();
+      for (int i = 0; i < EPL; i += 4) {
+        if (p0 + i < W) {
+          const float4 v = __ldcg(reinterpret_cast<const float4*>(row + p0 + i));
+          s[i] = v.x; s[i + 1] = v.y; s[i + 2] = v.z; s[i + 3] = v.w;
+        } else {
+          s[i] = s[i + 1] = s[i + 2] = s[i + 3] = neg_inf();
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) s[i] = (p0 + i < W) ? __ldcg(row + p0 + i) : neg_inf();
+    }
+    const int nv = min(n_valid_pages(p.lens[b], p.bs), W);
+    float* srow = s_row_all[threadIdx.x >> 5];
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) srow[p0 + i] = s[i];
+    __syncwarp();
 
     // lse over all W pages (coverage.py:179-195): -inf entries contribute 0
     float m = -1e20f;
@@ -265,14 +337,14 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(Se
     if (p.mode == CVSA_MODE_LAZY && p.has_cache && p.cached_idx) {
       const int nc = min(max(p.cached_n[bh], 0), p.cached_stride);
       const float lse_c =
-          lse_list_warp(row, W, p.cached_idx + (int64_t)bh * p.cached_stride, nc);
+          lse_list_smem(srow, W, p.cached_idx + (int64_t)bh * p.cached_stride, nc);
       const float cov = expf(lse_c - lse_all);
       const bool acc = cov >= p.tau;
       if (lane == 0) {
         if (p.cached_accept) p.cached_accept[bh] = acc ? 1 : 0;
         if (p.cached_cov) p.cached_cov[bh] = cov;
         if (!acc) atomicAdd(&s_rej, 1);
-        count_head(p, acc);
+        count(acc);
       }
     }
 
@@ -296,16 +368,54 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(Se
       for (int i = 0; i < EPL; ++i) key[i] = float_key(s[i]);
       uint32_t thr = 0;
       int take_eq = 0;
-      if (k > 0 && !all_cand) {
-        // largest T with #{candidates with key >= T} >= k, bit by bit
-#pragma unroll 1
-        for (int bit = 31; bit >= 0; --bit) {
-          const uint32_t c = thr | (1u << bit);
-          unsigned cnt = 0;
+      if (k > 0 && !all_cand && k <= kExtractMax) {
+        // T = the k-th largest candidate key: each lane sorts its keys in
+        // registers (non-candidates as 0, below every candidate key but NaN's,
+        // which leaves the k-th value unchanged), then k rounds take the warp
+        // maximum of the lanes' largest remaining keys; the lowest lane
+        // holding it drops that key
+        uint32_t kk[EPL];
 #pragma unroll
-          for (int i = 0; i < EPL; ++i) cnt += (cand[i] && key[i] >= c) ? 1u : 0u;
-          if ((int)__reduce_add_sync(0xffffffffu, cnt) >= k) thr = c;
+        for (int i = 0; i < EPL; ++i) kk[i] = cand[i] ? key[i] : 0u;
+        sort_asc<EPL>(kk);
+#pragma unroll 1
+        for (int r = 0; r < k; ++r) {
+          thr = __reduce_max_sync(0xffffffffu, kk[EPL - 1]);
+          const unsigned who = __ballot_sync(0xffffffffu, kk[EPL - 1] == thr);
+          if (lane == __ffs(who) - 1) {
+#pragma unroll
+            for (int i = EPL - 1; i > 0; --i) kk[i] = kk[i - 1];
+            kk[0] = 0u;
+          }
         }
+      } else if (k > 0 && !all_cand) {
+        // largest T with #{candidates with key >= T} >= k, bit by bit; the
+        // warp-wide count is a sum of independent ballots. T lies between the
+        // smallest and largest candidate key, so the bits above their highest
+        // differing bit are fixed from the start.
+        uint32_t kmin = 0xffffffffu, kmax = 0;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i)
+          if (cand[i]) {
+            kmin = min(kmin, key[i]);
+            kmax = max(kmax, key[i]);
+          }
+        kmin = __reduce_min_sync(0xffffffffu, kmin);
+        kmax = __reduce_max_sync(0xffffffffu, kmax);
+        const int top = 31 - __clz(kmin ^ kmax);  // -1 when all keys are equal
+        thr = top >= 0 ? (kmax & ~((2u << top) - 1u)) : kmax;
+        if (top == 31) thr = 0;
+#pragma unroll 1
+        for (int bit = top; bit >= 0; --bit) {
+          const uint32_t c = thr | (1u << bit);
+          int cnt = 0;
+#pragma unroll
+          for (int i = 0; i < EPL; ++i)
+            cnt += __popc(__ballot_sync(0xffffffffu, cand[i] && key[i] >= c));
+          if (cnt >= k) thr = c;
+        }
+      }
+      if (k > 0 && !all_cand) {
         unsigned gt = 0;
 #pragma unroll
         for (int i = 0; i < EPL; ++i) gt += (cand[i] && key[i] > thr) ? 1u : 0u;
@@ -377,10 +487,17 @@ __global__ void __launch_bounds__(kWarpSelWarps * 32) select_gate_warp_kernel(Se
         if (p.comp_cnt) p.comp_cnt[bh] = acc ? 0 : (nv + p.comp_chunk - 1) / p.comp_chunk;
         if (p.mode == CVSA_MODE_SCORE) {
           if (!acc) atomicAdd(&s_rej, 1);
-          if (!p.lazy_stats) count_head(p, acc);
+          if (!p.lazy_stats) count(acc);
         }
       }
     }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && p.counters && s_heads[0]) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_ACCEPT]),
+              (unsigned long long)s_heads[1]);
+    atomicAdd(reinterpret_cast<unsigned long long*>(&p.counters[CVSA_CTR_HEAD_TOTAL]),
+              (unsigned long long)s_heads[0]);
   }
   finish_select<NT>(p, s_rej, s_flag, wsum);
   pdl_launch_dependents();

@@ -165,6 +165,62 @@ def test_config2_properties_full_size(cuda, config2_cpu):
     assert abs(st["effective_budget_pct"] - 28 / 512 * 100) < 1e-9
 
 
+@pytest.fixture(scope="module")
+def config3_cpu():
+    return synthetic.config3()
+
+
+def test_config3_scoring_step_vs_oracle(cuda, config3_cpu):
+    """Full config 3 (one 128K sequence, 8192 pages): heads spread over every CTA of
+    the stream and rejected heads over dozens of them; selection bit-exact,
+    decisions exact, output in tolerance."""
+    wl = config3_cpu
+    d = wl.to(cuda)
+    be = CVSABackend(8, 32, 128, 16, num_layers=1, budget_pct=wl.budget_pct,
+                     coverage_threshold=wl.tau, sink_pages=1, local_pages=2,
+                     keep_page_scores=True)
+    out = be(d.q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+    torch.set_num_threads(8)
+    r = R.scoring_step(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 8, 4, 16,
+                       wl.budget_pct, wl.tau, 1, 2)
+    gs = be._layers[0].scores.cpu()
+    fin = torch.isfinite(r["page_scores"])
+    assert (gs[fin] - r["page_scores"][fin]).abs().max() < 2e-5 * max(1.0, float(
+        r["page_scores"][fin].abs().max()))
+    gap = R.topk_gap(r["page_scores"], wl.context_lens, 16, int(r["budget"]), 1, 2)
+    gi, gn = be.cached_selection(0)
+    G_sets, O_sets = sel_sets(gi.cpu(), gn.cpu()), sel_sets(r["page_indices"], r["n_per_head"])
+    mism = [h for h in range(8) if G_sets[0][h] != O_sets[0][h]]
+    assert all(gap[0, h] < 4e-5 for h in mism), mism
+    assert len(mism) == 0, f"{len(mism)} near-tie selection differences"
+    acc = be._last_accept_mask[0].cpu()
+    margin = R.coverage_margin(r["coverage"], wl.tau)
+    assert torch.equal(acc[margin > 1e-5], r["accept"][margin > 1e-5])
+    assert 1 <= int((~r["accept"]).sum()) <= 7      # the calibrated mix: some heads recover
+    _close(out, r["output"], torch.bfloat16)
+    # reuse step on the cached selection = the draft over that selection
+    be._step = 1
+    out_r = be(d.q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+    draft = SD.sparse_decode(d.q, d.k_cache, d.v_cache, d.block_tables, gi, gn, d.context_lens,
+                             8, 4, 16)
+    assert torch.equal(out_r, draft)
+
+
+def test_config3_every_head_recovers_equals_dense(cuda, config3_cpu):
+    """tau > 1 at 128K: all 8 heads take all 8192 pages, each split over many CTAs."""
+    d = config3_cpu.to(cuda)
+    dense = DenseAttentionBackend(8, 32, 128, 16)(d.q, d.k_cache, d.v_cache, d.block_tables,
+                                                  d.context_lens, 0)
+    be = CVSABackend(8, 32, 128, 16, num_layers=1, budget_pct=0.05, coverage_threshold=1.01,
+                     sink_pages=1, local_pages=2)
+    out = be(d.q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+    assert not be._last_accept_mask[0].any()
+    _close(out, dense, torch.bfloat16)
+    ref = R.dense_decode(config3_cpu.q, config3_cpu.k_cache, config3_cpu.v_cache,
+                         config3_cpu.block_tables, config3_cpu.context_lens, 8, 4, 16)
+    _close(out, ref, torch.bfloat16)
+
+
 def test_step_is_graph_capturable_and_deterministic(cuda):
     wl = synthetic.small(seed=9, B=4, Hq=32, Hkv=8, D=128, ctx=(4096, 2000, 8192, 100))
     d = wl.to(cuda)
