@@ -74,7 +74,8 @@ struct SelectParams {
   uint8_t* cached_accept;     // [B, Hkv] or null
   float* cached_cov;
   // batch-global decision & statistics
-  int32_t* sync_ctr;          // [2] zeroed: CTA-done count, reject count
+  int32_t* sync_ctr;          // [2] zeroed, 8-byte aligned: one 64-bit counter
+                              // (CTAs done | rejected heads << 32)
   int32_t* decision;          // [1] out: bit0 all cached heads accepted
   int64_t* counters;          // [CVSA_NUM_COUNTERS] or null
   int mode;                   // CVSA_MODE_SCORE / CVSA_MODE_LAZY / -1 (plain select)

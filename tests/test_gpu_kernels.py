@@ -102,10 +102,30 @@ def _select_cases():
     # -0.0 / +0.0 and denormals
     s = torch.tensor([[[0.0, -0.0, 1e-40, -1e-40, 0.0, 3.0, -0.0, 1e-40]]])
     cases.append((s, torch.tensor([128], dtype=torch.int32), 3, 0, 0))
+    # long tables (one CTA of 1024 threads per head): random, ragged
+    s = torch.randn(2, 3, 2000, generator=g)
+    cl = torch.tensor([32000, 20000], dtype=torch.int32)
+    cases.append((s, cl, 100, 1, 2))
+    s = torch.randn(1, 2, 8192, generator=g) * 3
+    cases.append((s, torch.tensor([131072], dtype=torch.int32), 409, 1, 2))
+    # 12000 pages with heavy ties
+    s = torch.randint(0, 8, (1, 4, 12000), generator=g).float()
+    cases.append((s, torch.tensor([190000], dtype=torch.int32), 600, 1, 2))
+    # scores on a 0.02 grid: a few equal keys inside the k-th key's value bin
+    s = torch.round(torch.randn(2, 3, 4096, generator=g) * 50) / 50
+    cases.append((s, torch.tensor([65536, 40000], dtype=torch.int32), 204, 1, 2))
+    # 16384 pages (16 per thread)
+    s = torch.randn(1, 2, 16384, generator=g)
+    cases.append((s, torch.tensor([262144], dtype=torch.int32), 819, 1, 2))
+    # non-finite candidate scores: -inf inside the valid range and one +inf
+    s = torch.randn(1, 2, 3000, generator=g)
+    s[0, 0, 100:400] = float("-inf")
+    s[0, 1, 1234] = float("inf")
+    cases.append((s, torch.tensor([48000], dtype=torch.int32), 150, 1, 2))
     return cases
 
 
-@pytest.mark.parametrize("ci", range(6))
+@pytest.mark.parametrize("ci", range(12))
 def test_select_bit_exact(cuda, ci):
     s, cl, budget, sink, local = _select_cases()[ci]
     nv = R.n_valid_pages(cl, 16)
