@@ -61,6 +61,7 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 // the softmax reference max is refreshed when a score passes it by more than
 // this (natural log units): probabilities stay below e^8 ~ 3e3
 constexpr float kRescaleGap = 8.0f;
+constexpr int kMaxQSlots = 8;  // heads whose query rows a CTA stages in shared memory
 
 enum : int { kKindEmpty = 0, kKindList = 1, kKindRange = 2, kKindRangeSkip = 3 };
 
@@ -111,6 +112,9 @@ struct StreamArgs {
   int nc, stages, meta_cap;
   // shared-memory carve-up, byte offsets from the 1024-aligned base
   int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+  // the query rows of a CTA's first q_slots heads are copied into shared
+  // memory at the start (one bulk copy per head on the mbarrier at off_qbar)
+  int off_qbar, off_q, q_slots;
   float scale;
 };
 
@@ -328,7 +332,8 @@ __device__ __forceinline__ int64_t partial_slot(int h, int c, int k, int nc) {
 // reduction of cvsa/kernels/sparse_decode.py:577-606 (maximum over the
 // partials, weights exp(m_t - M), sums) at warp scale. Lane t holds partial
 // t's (m, l) (one load round for up to 32 partials); the columns of kU
-// partials are in flight together.
+// partials are in flight together, the first kU issued with the (m, l) loads
+// (they do not depend on M), so up to kU partials cost one round trip.
 template <int D, class RowOf>
 __device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_of, float& M,
                            float& L, float (&acc)[D / 32]) {
@@ -339,6 +344,16 @@ __device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_
   if (lane < np) {
     m0 = __ldcg(&pml[row_of(lane) * 2]);
     l0 = __ldcg(&pml[row_of(lane) * 2 + 1]);
+  }
+  float ov0[kU][PL];
+#pragma unroll
+  for (int u = 0; u < kU; ++u) {
+    if (u < np) {
+      load_vec_cg<PL>(po + row_of(u) * D + lane * PL, ov0[u]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < PL; ++i) ov0[u][i] = 0.f;
+    }
   }
   M = m0;
   for (int t = lane + 32; t < np; t += 32) M = fmaxf(M, __ldcg(&pml[row_of(t) * 2]));
@@ -359,13 +374,20 @@ __device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_
     const int cnt = min(32, np - t0);
     for (int v0 = 0; v0 < cnt; v0 += kU) {
       float ov[kU][PL];
+      if (t0 == 0 && v0 == 0) {
 #pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        if (v0 + u < cnt) {
-          load_vec_cg<PL>(po + row_of(t0 + v0 + u) * D + lane * PL, ov[u]);
-        } else {
+        for (int u = 0; u < kU; ++u)
 #pragma unroll
-          for (int i = 0; i < PL; ++i) ov[u][i] = 0.f;
+          for (int i = 0; i < PL; ++i) ov[u][i] = ov0[u][i];
+      } else {
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          if (v0 + u < cnt) {
+            load_vec_cg<PL>(po + row_of(t0 + v0 + u) * D + lane * PL, ov[u]);
+          } else {
+#pragma unroll
+            for (int i = 0; i < PL; ++i) ov[u][i] = 0.f;
+          }
         }
       }
 #pragma unroll
@@ -406,7 +428,13 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   const int C = gridDim.x, c = blockIdx.x;
   const int nthreads = blockDim.x;
 
+  uint64_t* qbar = reinterpret_cast<uint64_t*>(sm + a.off_qbar);
+  T* qs = reinterpret_cast<T*>(sm + a.off_q);
   for (int i = tid; i < kMiscWords; i += nthreads) misc[i] = 0;
+  if (tid == 0 && a.q_slots > 0) {
+    mbar_init(qbar, 1);
+    fence_mbar_init();
+  }
   pdl_wait();
 
   // ---- head table: kind, context length and the exclusive prefix of w_h ----
@@ -553,6 +581,20 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     }
     hhi = lo;
   }
+  // stage the query rows of the first heads: a head switch then reads them
+  // from shared memory instead of waiting behind the page stream in DRAM
+  const int nq = hhi >= hlo ? min(hhi - hlo + 1, a.q_slots) : 0;
+  const int q_elems = G * D;
+  if (tid == 0 && nq > 0) {
+    mbar_arrive_expect_tx(qbar, (uint32_t)(nq * q_elems * (int)sizeof(T)));
+    const uint64_t qpol = make_evict_first_policy();
+    for (int i = 0; i < nq; ++i) {
+      const int bh = a.h_base + hlo + i;
+      const T* src = reinterpret_cast<const T*>(a.q) +
+                     ((int64_t)(bh / a.hkv) * a.hq + (int64_t)(bh % a.hkv) * G) * D;
+      bulk_load(qs + (size_t)i * q_elems, src, (uint32_t)(q_elems * sizeof(T)), qbar, qpol);
+    }
+  }
 
   if (warp == NC) {
     // ======================= page-descriptor producer =======================
@@ -690,11 +732,26 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
         l_part[n][i] = 0.f;
       }
   };
-  // Q^T as the B operand of S^T = K Q^T: b0 = Q[g][16 ks + 2 tq ..], b1 = +8
-  auto load_q = [&](int h) {
-    const int bh = a.h_base + h;
-    const int b = bh / a.hkv, hh = bh % a.hkv;
-    const T* qp = reinterpret_cast<const T*>(a.q) + ((int64_t)b * a.hq + (int64_t)hh * G) * D;
+  // Q^T as the B operand of S^T = K Q^T: b0 = Q[g][16 ks + 2 tq ..], b1 = +8,
+  // from the staged copy where there is one
+  bool q_staged = false;
+  auto load_q = [&](int h) -> bool {
+    const T* qp;
+    if (h - hlo < nq) {
+      if (!q_staged) {
+        if (!mbar_wait_bounded(qbar, 0)) {
+          vmisc[kMiscFail] = 1;
+          set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
+          return false;
+        }
+        q_staged = true;
+      }
+      qp = qs + (size_t)(h - hlo) * q_elems;
+    } else {
+      const int bh = a.h_base + h;
+      const int b = bh / a.hkv, hh = bh % a.hkv;
+      qp = reinterpret_cast<const T*>(a.q) + ((int64_t)b * a.hq + (int64_t)hh * G) * D;
+    }
 #pragma unroll
     for (int n = 0; n < GR; ++n) {
       const int g = n * 8 + gq;
@@ -709,6 +766,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
         qb[ks][n][1] = hi;
       }
     }
+    return true;
   };
 
   // Write the state of head h as this consumer's partial, rescaled from the
@@ -764,7 +822,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
       reset_state();
     }
     if (!have_q) {
-      load_q(h);
+      if (!load_q(h)) break;
       have_q = true;
     }
     cp_async_wait_dyn(S - 1);
@@ -883,12 +941,16 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     flush_head(h);
     reset_state();
   }
-  // no copy may still be landing in shared memory past this point; with none
-  // in flight, a fence is cheap: it makes this warp's partials visible to the
-  // CTA that merges a split head before this CTA takes its ticket
+  // no copy may still be landing in shared memory past this point (the
+  // partials are read by this CTA only, after the barrier below)
   asm volatile("cp.async.wait_all;" ::: "memory");
-  __threadfence();
   }  // consumers
+  // the staged query rows have landed even if no consumer read them (no
+  // bulk copy may outlive the CTA)
+  if (tid == 0 && nq > 0 && !mbar_wait_bounded(qbar, 0)) {
+    vmisc[kMiscFail] = 1;
+    set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
+  }
 
   // ============================ finish the heads ============================
   // Every warp is done streaming (no copies in flight): the partials written
@@ -924,24 +986,31 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
           __stcg(&a.cpart_ml[row * 2], M);
           __stcg(&a.cpart_ml[row * 2 + 1], L);
         }
-        __threadfence();
       }
     }
   }
+  // Tickets: the barrier orders every warp's CTA-partial stores before
+  // thread 0's fence, which publishes them before its ticket (both tickets in
+  // flight together); the winner's fence orders the other CTAs' partials
+  // before its reads.
   __syncthreads();
   int* won = misc + kMiscWon;
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      const int h = split_head(i);
-      won[i] = 0;
-      if (h < 0) continue;
+    const int hs0 = split_head(0), hs1 = split_head(1);
+    won[0] = won[1] = 0;
+    if (hs0 >= 0 || hs1 >= 0) {
       __threadfence();
-      const int t = atomicAdd(&a.head_done[a.h_base + h], 1);
-      if (t == last_cta(h) - first_cta(h)) {
-        won[i] = 1;
-        a.head_done[a.h_base + h] = 0;
-        __threadfence();
+      const int t0 = hs0 >= 0 ? atomicAdd(&a.head_done[a.h_base + hs0], 1) : -1;
+      const int t1 = hs1 >= 0 ? atomicAdd(&a.head_done[a.h_base + hs1], 1) : -1;
+      if (hs0 >= 0 && t0 == last_cta(hs0) - first_cta(hs0)) {
+        won[0] = 1;
+        a.head_done[a.h_base + hs0] = 0;
       }
+      if (hs1 >= 0 && t1 == last_cta(hs1) - first_cta(hs1)) {
+        won[1] = 1;
+        a.head_done[a.h_base + hs1] = 0;
+      }
+      if (won[0] | won[1]) __threadfence();
     }
   }
   __syncthreads();
@@ -1025,6 +1094,20 @@ cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
   a.off_kind = pl.off_kind;
   a.off_span = pl.off_span;
   a.off_misc = pl.off_misc;
+  // query-row staging in the shared memory the plan leaves over
+  {
+    const size_t qbytes = (size_t)a.G * D * sizeof(T);
+    size_t off = up((size_t)pl.smem - 1024, 16);
+    a.off_qbar = (int)off;
+    off += 16;
+    a.off_q = (int)off;
+    int slots = 0;
+    const bool q_aligned = (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && qbytes % 16 == 0;
+    if (q_aligned && off + qbytes + 1024 <= (size_t)kSmemCap)
+      slots = (int)(((size_t)kSmemCap - 1024 - off) / qbytes);
+    a.q_slots = slots < kMaxQSlots ? slots : kMaxQSlots;
+    pl.smem = (int)(off + (size_t)a.q_slots * qbytes + 1024);
+  }
   static bool attr_set[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
