@@ -220,6 +220,13 @@ __device__ __forceinline__ void load_vec_cg(const float* p, float (&v)[N]) {
   }
 }
 
+// One partial row in global scratch (read with L1 bypassed: lines there may
+// predate this launch's stores).
+struct PartRow {
+  const float* o;   // D values
+  const float* ml;  // (m, l)
+};
+
 template <int N>
 __device__ __forceinline__ void store_vec_cg(float* p, const float (&v)[N]) {
   if constexpr (N % 4 == 0) {
@@ -327,7 +334,7 @@ __device__ __forceinline__ int64_t partial_slot(int h, int c, int k, int nc) {
   return (int64_t)(h + c) * nc + k;
 }
 
-// Merge np partial rows, the t-th at row index row_of(t) of (po, pml), in
+// Merge np partial rows, the t-th at row_of(t) (a PartRow), in
 // order t = 0..np-1 (deterministic), into (M, L, acc): the split-decode
 // reduction of cvsa/kernels/sparse_decode.py:577-606 (maximum over the
 // partials, weights exp(m_t - M), sums) at warp scale. Lane t holds partial
@@ -335,28 +342,28 @@ __device__ __forceinline__ int64_t partial_slot(int h, int c, int k, int nc) {
 // partials are in flight together, the first kU issued with the (m, l) loads
 // (they do not depend on M), so up to kU partials cost one round trip.
 template <int D, class RowOf>
-__device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_of, float& M,
-                           float& L, float (&acc)[D / 32]) {
+__device__ void merge_rows(int np, RowOf row_of, float& M, float& L, float (&acc)[D / 32]) {
   constexpr int PL = D / 32;
   constexpr int kU = PL >= 8 ? 4 : 32 / PL;
   const int lane = threadIdx.x & 31;
   float m0 = neg_inf(), l0 = 0.f;
   if (lane < np) {
-    m0 = __ldcg(&pml[row_of(lane) * 2]);
-    l0 = __ldcg(&pml[row_of(lane) * 2 + 1]);
+    const PartRow r = row_of(lane);
+    m0 = __ldcg(r.ml);
+    l0 = __ldcg(r.ml + 1);
   }
   float ov0[kU][PL];
 #pragma unroll
   for (int u = 0; u < kU; ++u) {
     if (u < np) {
-      load_vec_cg<PL>(po + row_of(u) * D + lane * PL, ov0[u]);
+      load_vec_cg<PL>(row_of(u).o + lane * PL, ov0[u]);
     } else {
 #pragma unroll
       for (int i = 0; i < PL; ++i) ov0[u][i] = 0.f;
     }
   }
   M = m0;
-  for (int t = lane + 32; t < np; t += 32) M = fmaxf(M, __ldcg(&pml[row_of(t) * 2]));
+  for (int t = lane + 32; t < np; t += 32) M = fmaxf(M, __ldcg(row_of(t).ml));
   M = warp_max(M);
   L = 0.f;
 #pragma unroll
@@ -366,8 +373,8 @@ __device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_
     float w = 0.f;
     const int t = t0 + lane;
     if (t < np) {
-      const float mt = t0 == 0 ? m0 : __ldcg(&pml[row_of(t) * 2]);
-      const float lt = t0 == 0 ? l0 : __ldcg(&pml[row_of(t) * 2 + 1]);
+      const float mt = t0 == 0 ? m0 : __ldcg(row_of(t).ml);
+      const float lt = t0 == 0 ? l0 : __ldcg(row_of(t).ml + 1);
       w = (mt == neg_inf()) ? 0.f : expf(mt - M);
       L += lt * w;
     }
@@ -383,7 +390,7 @@ __device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_
 #pragma unroll
         for (int u = 0; u < kU; ++u) {
           if (v0 + u < cnt) {
-            load_vec_cg<PL>(po + row_of(t0 + v0 + u) * D + lane * PL, ov[u]);
+            load_vec_cg<PL>(row_of(t0 + v0 + u).o + lane * PL, ov[u]);
           } else {
 #pragma unroll
             for (int i = 0; i < PL; ++i) ov[u][i] = 0.f;
@@ -401,13 +408,65 @@ __device__ void merge_rows(const float* po, const float* pml, int np, RowOf row_
   L = warp_sum(L);
 }
 
+// Where the partials of one merge live. Consumer partials of head h in CTA
+// c: the t-th comes from consumer kk = kf + t (every slice non-empty) or the
+// consumer of local position p0 + t (slices of at most one position), slot
+// (h + c) NC + kk. CTA partials of head h: the t-th at row (h + fc + t) of
+// the CTA-partial scratch.
+struct MergeCtx {
+  int c, NC, nloc, G;
+  const float* part_o;
+  const float* part_ml;
+  float* cpart_o;
+  float* cpart_ml;
+};
+struct RowSrc {
+  int cpart, h, g, np;
+  int kf, p0;  // consumer partials
+  int fc;      // CTA partials
+};
+template <int D>
+__device__ __forceinline__ PartRow part_row(const MergeCtx& x, const RowSrc& r, int t) {
+  if (r.cpart) {
+    const int64_t row = (int64_t)(r.h + r.fc + t) * x.G + r.g;
+    return PartRow{x.cpart_o + row * D, x.cpart_ml + row * 2};
+  }
+  // (32-bit: nloc * NC stays far below 2^31)
+  const int kk = x.nloc >= x.NC ? r.kf + t : ((r.p0 + t + 1) * x.NC - 1) / x.nloc;
+  const int64_t row = ((int64_t)(r.h + x.c) * x.NC + kk) * x.G + r.g;
+  return PartRow{x.part_o + row * D, x.part_ml + row * 2};
+}
+
+enum : int { kEmitFinish = 0, kEmitCtaPartial = 1 };
+
+// One warp: merge the partials of r (none: the empty state) and either
+// finish query row r.g of head r.h or store it as this CTA's partial of the
+// head (inlined: an out-of-line copy measured slower).
+template <int D>
+__device__ __forceinline__ void merge_emit(const StreamArgs& a, MergeCtx x, RowSrc r, int emit,
+                                        int kind) {
+  constexpr int PL = D / 32;
+  float M, L, acc[PL];
+  merge_rows<D>(r.np, [&](int t) { return part_row<D>(x, r, t); }, M, L, acc);
+  if (emit == kEmitFinish) {
+    finish_row<D>(a, a.h_base + r.h, kind, r.g, M, L, acc);
+  } else {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)(r.h + x.c) * x.G + r.g;
+    store_vec_cg<PL>(x.cpart_o + row * D + lane * PL, acc);
+    if (lane == 0) {
+      __stcg(&x.cpart_ml[row * 2], M);
+      __stcg(&x.cpart_ml[row * 2 + 1], L);
+    }
+  }
+}
+
 template <typename T, int D, int GR>
 __global__ void __launch_bounds__((max_consumers<D, GR>() + 1) * 32, 1)
 stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   constexpr int kSub = D / 64;                         // 64-column slices
   constexpr int kTile = kBS * 128;                     // one swizzled slice of a page
   constexpr uint32_t kStageBytes = 2 * kSub * kTile;   // K and V of one page
-  constexpr int PL = D / 32;                           // output columns per lane
   constexpr int kRowChunks = D / 8;                    // 16-byte chunks per token row
   constexpr int kCopies = kBS * kRowChunks / 32;       // cp.async per lane per tensor and page
 
@@ -545,16 +604,15 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   // this grid's completion before reading anything it wrote)
   pdl_launch_dependents();
 
+  const MergeCtx mctx{c, NC, nloc, G, a.part_o, a.part_ml, a.cpart_o, a.cpart_ml};
   // Empty heads (no pages) are finished from the empty state by CTA h % C,
   // one warp per query row.
   auto finish_empty_heads = [&]() {
-    float z[PL];
-#pragma unroll
-    for (int i = 0; i < PL; ++i) z[i] = 0.f;
     const int mine = c < H ? (H - 1 - c) / C + 1 : 0;
     for (int u = warp; u < mine * G; u += nthreads / 32) {
       const int h = c + (u / G) * C, g = u % G;
-      if (empty_head(h)) finish_row<D>(a, a.h_base + h, kindv[h], g, neg_inf(), 0.f, z);
+      if (empty_head(h))
+        merge_emit<D>(a, mctx, RowSrc{0, h, g, 0, 0, 0, 0}, kEmitFinish, kindv[h]);
     }
   };
   if (P == 0) {
@@ -596,12 +654,24 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     }
   }
 
+  // Consumer k streams the contiguous local positions [slice(k), slice(k+1))
+  // (sizes differ by at most one), so it meets few heads; they are handed out
+  // in issue order j = k + q NC (its q-th position), which the producer
+  // resolves in order.
+  // (32-bit: P < 2^31, so nloc <= P / gridDim.x + 1 and nloc * NC < 2^31)
+  auto slice_lo = [&](int kk) -> int { return nloc * kk / NC; };
+  auto consumer_of = [&](int p) -> int { return ((p + 1) * NC - 1) / nloc; };
+  const int qmax = (nloc + NC - 1) / NC;  // longest slice
+  const int njobs = qmax * NC;
+
   if (warp == NC) {
     // ======================= page-descriptor producer =======================
-    for (int xb = 0; xb < nloc; xb += 32) {
-      const int p = xb + lane;  // local position
+    for (int xb = 0; xb < njobs; xb += 32) {
+      const int j = xb + lane;  // issue index
+      const int kk = j % NC, qq = j / NC;
+      const int p = slice_lo(kk) + qq;  // local position
       int blk = -1, nt = 0;
-      if (p < nloc) {
+      if (j < njobs && p < slice_lo(kk + 1)) {
         const int x = Xc + p;
         int lo = 0, hi = H - 1;  // largest h with pref[h] <= x (a non-empty head)
         while (lo < hi) {
@@ -637,16 +707,17 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
             }
           }
         }
-        // the ring entry is free once its previous position has been read
-        if (p >= MR && !spin_until_ge(vmisc + kMiscCons + p % NC, p - MR + 1, vmisc + kMiscFail)) {
+        // the ring entry is free once its previous index (same consumer) has
+        // been read
+        if (j >= MR && !spin_until_ge(vmisc + kMiscCons + kk, j - MR + 1, vmisc + kMiscFail)) {
           vmisc[kMiscFail] = 1;
           set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
         }
-        meta[p % MR] = make_int2(blk, nt);
+        meta[j % MR] = make_int2(blk, nt);
       }
       __threadfence_block();
       __syncwarp();
-      if (lane == 0) vmisc[kMiscProd] = min(xb + 32, nloc);
+      if (lane == 0) vmisc[kMiscProd] = min(xb + 32, njobs);
       if (vmisc[kMiscFail]) break;
     }
     commit_heads();
@@ -675,9 +746,10 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   // copy the page of my q-th position into stage q % S (a group is committed
   // even when nothing is copied, so group counting stays uniform); the
   // descriptor is {block, tokens | kv head << 8}
+  const int my_lo = slice_lo(k), nmine = slice_lo(k + 1) - my_lo;
   auto issue = [&](int q) -> bool {
     const int j = k + q * NC;
-    if (j < nloc) {
+    if (q < nmine) {
       if (lane == 0 && !spin_until_ge(vmisc + kMiscProd, j + 1, vmisc + kMiscFail)) {
         vmisc[kMiscFail] = 1;
         set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
@@ -805,16 +877,24 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   };
 
   // ---- main loop over my positions ----
-  const int nmine = nloc > k ? (nloc - k + NC - 1) / NC : 0;
   bool ok = true;
   for (int q = 0; q < S - 1 && ok; ++q) ok = issue(q);
-  int h = hlo;
+  int h = hlo;  // the head of my first position (a non-empty head)
+  if (nmine > 0) {
+    int lo = hlo, hi = hhi;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (pref[mid] <= Xc + my_lo) lo = mid;
+      else hi = mid - 1;
+    }
+    h = lo;
+  }
   bool have_q = false;
   reset_state();
   for (int q = 0; q < nmine && ok; ++q) {
     ok = issue(q + S - 1);
     if (!ok) break;
-    const int x = Xc + k + q * NC;
+    const int x = Xc + my_lo + q;
     while (x >= pref[h + 1]) {  // heads that end before x are done for me
       flush_head(h);
       ++h;
@@ -936,11 +1016,8 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     }
     __syncwarp();  // the stage is refilled by the next issue
   }
-  // heads after my last position (and the current one) are done for me
-  for (; ok && h <= hhi; ++h) {
-    flush_head(h);
-    reset_state();
-  }
+  // the head of my last position is done for me
+  if (ok && nmine > 0) flush_head(h);
   // no copy may still be landing in shared memory past this point (the
   // partials are read by this CTA only, after the barrier below)
   asm volatile("cp.async.wait_all;" ::: "memory");
@@ -957,37 +1034,34 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   // by this CTA's consumers are visible to the whole CTA after the barrier.
   __syncthreads();
   if (vmisc[kMiscFail]) return;  // a copy never arrived: leave the outputs alone
-  // Merges, one warp per query row. Heads inside this CTA's range are merged
-  // from its consumers' partials and finished. A head split over CTAs (only
-  // this CTA's first and last head can be) is first merged over this CTA's
-  // consumers into one CTA partial (slot head + CTA); the last of its CTAs to
-  // get here (ticket per head, no spin) merges the CTA partials in CTA order.
+  // Merges, one warp per query row. A head split over CTAs (only this CTA's
+  // first and last head can be) is first merged over this CTA's consumers
+  // into one CTA partial (slot head + CTA); the last of its CTAs to get here
+  // (ticket per head, no spin) merges the CTA partials in CTA order. The
+  // split heads' CTA partials are written first, so thread 0's tickets are in
+  // flight while the other warps merge and finish the heads inside the range.
   auto split_head = [&](int i) -> int {  // this CTA's first (0) / last (1) head if split
     const int h = i == 0 ? hlo : hhi;
     if (hlo > hhi || (i == 1 && hhi == hlo) || empty_head(h) || first_cta(h) == last_cta(h))
       return -1;
     return h;
   };
-  {
-    const int nrow = (hhi - hlo + 1) * G;
-    for (int u = warp; u < nrow; u += nthreads / 32) {
-      const int h = hlo + u / G, g = u % G;
-      if (empty_head(h)) continue;
-      float M, L, acc[PL];
-      merge_rows<D>(a.part_o, a.part_ml, NC,
-                    [&](int t) -> int64_t { return partial_slot(h, c, t, NC) * G + g; }, M, L,
-                    acc);
-      if (first_cta(h) == last_cta(h)) {
-        finish_row<D>(a, a.h_base + h, kindv[h], g, M, L, acc);
-      } else {
-        const int64_t row = (int64_t)(h + c) * G + g;
-        store_vec_cg<PL>(a.cpart_o + row * D + lane * PL, acc);
-        if (lane == 0) {
-          __stcg(&a.cpart_ml[row * 2], M);
-          __stcg(&a.cpart_ml[row * 2 + 1], L);
-        }
-      }
-    }
+  const int sh0 = split_head(0), sh1 = split_head(1);
+  const int nwarps = nthreads / 32;
+  // The consumers whose slices meet head h (a non-empty head of this CTA):
+  // consumer_of(p0) .. consumer_of(p1 - 1) when every slice is non-empty
+  // (nloc >= NC); otherwise each non-empty slice is one position, and the
+  // t-th partial is that of position p0 + t.
+  auto cons_src = [&](int h, int g) -> RowSrc {
+    const int p0 = max(pref[h], Xc) - Xc, p1 = min(pref[h + 1], Xe) - Xc;
+    const int kf = consumer_of(p0);
+    const int np = nloc >= NC ? consumer_of(p1 - 1) - kf + 1 : p1 - p0;
+    return RowSrc{0, h, g, np, kf, p0, 0};
+  };
+  for (int u = warp; u < 2 * G; u += nwarps) {
+    const int h = u < G ? sh0 : sh1, g = u % G;
+    if (h < 0) continue;
+    merge_emit<D>(a, mctx, cons_src(h, g), kEmitCtaPartial, kindv[h]);
   }
   // Tickets: the barrier orders every warp's CTA-partial stores before
   // thread 0's fence, which publishes them before its ticket (both tickets in
@@ -995,34 +1069,41 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   // before its reads.
   __syncthreads();
   int* won = misc + kMiscWon;
-  if (tid == 0) {
-    const int hs0 = split_head(0), hs1 = split_head(1);
-    won[0] = won[1] = 0;
-    if (hs0 >= 0 || hs1 >= 0) {
-      __threadfence();
-      const int t0 = hs0 >= 0 ? atomicAdd(&a.head_done[a.h_base + hs0], 1) : -1;
-      const int t1 = hs1 >= 0 ? atomicAdd(&a.head_done[a.h_base + hs1], 1) : -1;
-      if (hs0 >= 0 && t0 == last_cta(hs0) - first_cta(hs0)) {
-        won[0] = 1;
-        a.head_done[a.h_base + hs0] = 0;
+  if (warp == 0) {
+    if (tid == 0) {
+      won[0] = won[1] = 0;
+      if (sh0 >= 0 || sh1 >= 0) {
+        __threadfence();
+        const int t0 = sh0 >= 0 ? atomicAdd(&a.head_done[a.h_base + sh0], 1) : -1;
+        const int t1 = sh1 >= 0 ? atomicAdd(&a.head_done[a.h_base + sh1], 1) : -1;
+        if (sh0 >= 0 && t0 == last_cta(sh0) - first_cta(sh0)) {
+          won[0] = 1;
+          a.head_done[a.h_base + sh0] = 0;
+        }
+        if (sh1 >= 0 && t1 == last_cta(sh1) - first_cta(sh1)) {
+          won[1] = 1;
+          a.head_done[a.h_base + sh1] = 0;
+        }
+        if (won[0] | won[1]) __threadfence();
       }
-      if (hs1 >= 0 && t1 == last_cta(hs1) - first_cta(hs1)) {
-        won[1] = 1;
-        a.head_done[a.h_base + hs1] = 0;
-      }
-      if (won[0] | won[1]) __threadfence();
+    }
+  } else {
+    // heads inside this CTA's range: merge over the consumers and finish
+    const int nrow = (hhi - hlo + 1) * G;
+    for (int u = warp - 1; u < nrow; u += nwarps - 1) {
+      const int h = hlo + u / G, g = u % G;
+      if (h == sh0 || h == sh1 || empty_head(h)) continue;
+      merge_emit<D>(a, mctx, cons_src(h, g), kEmitFinish, kindv[h]);
     }
   }
   __syncthreads();
-  for (int u = warp; u < 2 * G; u += nthreads / 32) {
+  for (int u = warp; u < 2 * G; u += nwarps) {
     const int i = u / G, g = u % G;
     if (!won[i]) continue;
     const int h = i == 0 ? hlo : hhi;
     const int fc = first_cta(h);
-    float M, L, acc[PL];
-    merge_rows<D>(a.cpart_o, a.cpart_ml, last_cta(h) - fc + 1,
-                  [&](int t) -> int64_t { return (int64_t)(h + fc + t) * G + g; }, M, L, acc);
-    finish_row<D>(a, a.h_base + h, kindv[h], g, M, L, acc);
+    merge_emit<D>(a, mctx, RowSrc{1, h, g, last_cta(h) - fc + 1, 0, 0, fc}, kEmitFinish,
+                  kindv[h]);
   }
   finish_empty_heads();
 }
