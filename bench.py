@@ -442,7 +442,7 @@ def run_cvsa(args, ws, rank, local):
     peak, peak_kind = _peaks()
     achieved = score_bytes / (score_ms * 1e-3) / 1e9 if score_ms else None
     traffic = None
-    tfile = os.path.join(ROOT, "profiles", "score_pages_config2.md")
+    tfile = os.path.join(ROOT, "profiles", "score_stream_config2.md")
     if os.path.exists(tfile):
         for line in open(tfile):
             if line.startswith("traffic_bytes_per_launch:"):
