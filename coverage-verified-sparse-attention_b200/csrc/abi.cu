@@ -401,6 +401,12 @@ int cvsa_workspace_reset(void* workspace, size_t workspace_bytes, void* stream) 
                      "workspace memset");
 }
 
+int cvsa_step_decision_word(void* workspace, int32_t** word) {
+  if (!workspace || !word) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  *word = ws_select_sync(workspace) + 2;
+  return CVSA_OK;
+}
+
 int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
                      const cvsa_step_config_t* cfg, const cvsa_step_io_t* io, void* workspace,
                      size_t workspace_bytes, void* stream) {
@@ -414,6 +420,11 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   const int mode = cfg->mode;
   if (mode < CVSA_MODE_SCORE || mode > CVSA_MODE_DENSE)
     return fail(CVSA_ERR_INVALID, "unknown mode %d", mode);
+  const int phase = io ? io->phase : CVSA_PHASE_ALL;
+  if (phase < CVSA_PHASE_ALL || phase > CVSA_PHASE_ATTEND)
+    return fail(CVSA_ERR_INVALID, "unknown phase %d", phase);
+  if (phase != CVSA_PHASE_ALL && mode != CVSA_MODE_LAZY && mode != CVSA_MODE_SCORE)
+    return fail(CVSA_ERR_INVALID, "phases split LAZY and SCORE steps only");
   if (cfg->recovery != CVSA_RECOVERY_EXACT && cfg->recovery != CVSA_RECOVERY_NONE)
     return fail(CVSA_ERR_INVALID, "unknown recovery %d", cfg->recovery);
   if (cfg->budget < 0 || cfg->sink_pages < 0 || cfg->local_pages < 0)
@@ -475,6 +486,9 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
     return rec(CVSA_EV_ATTEND_END);
   }
 
+  // the two halves of a phased step share everything below; each launches its own
+  const bool run_select = phase != CVSA_PHASE_ATTEND;
+  const bool run_attend = phase != CVSA_PHASE_SELECT;
   float* scores = io->page_scores ? io->page_scores : reinterpret_cast<float*>(ws + L.scores);
   int32_t* sel_new = reinterpret_cast<int32_t*>(ws + L.sel);
   int32_t* n_new = reinterpret_cast<int32_t*>(ws + L.n);
@@ -485,10 +499,12 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   float* cov_c = reinterpret_cast<float*>(ws + L.cov_c);
   int32_t* sync = ws_select_sync(workspace);  // [0..1] select tickets, [2] decision
 
-  if ((st = rec(CVSA_EV_SCORE_BEGIN))) return st;
-  st = cuda_status(launch_score_pages(q, kv, scores, io->dev_error, s, pdl), "score launch");
-  if (st) return st;
-  if ((st = rec(CVSA_EV_SCORE_END))) return st;
+  if (run_select) {
+    if ((st = rec(CVSA_EV_SCORE_BEGIN))) return st;
+    st = cuda_status(launch_score_pages(q, kv, scores, io->dev_error, s, pdl), "score launch");
+    if (st) return st;
+    if ((st = rec(CVSA_EV_SCORE_END))) return st;
+  }
 
   SelectParams sp;
   memset(&sp, 0, sizeof(sp));
@@ -530,10 +546,16 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
     sp.comp_off = comp_off;
     sp.comp_chunk = attend_complement_chunk();
   }
-  if ((st = rec(CVSA_EV_SELECT_BEGIN))) return st;
-  st = cuda_status(launch_select_gate(sp, s, pdl), "select launch");
-  if (st) return st;
-  if ((st = rec(CVSA_EV_SELECT_END))) return st;
+  // a decision exchanged between the phases may turn a local reuse into a
+  // rescore: keep the complement items either way
+  sp.decision_external = phase != CVSA_PHASE_ALL;
+  if (run_select) {
+    if ((st = rec(CVSA_EV_SELECT_BEGIN))) return st;
+    st = cuda_status(launch_select_gate(sp, s, pdl), "select launch");
+    if (st) return st;
+    if ((st = rec(CVSA_EV_SELECT_END))) return st;
+  }
+  if (!run_attend) return CVSA_OK;
 
   ap.sel0 = io->cached_indices;
   ap.n0 = io->cached_n;

@@ -88,7 +88,8 @@ struct SelectParams {
   int32_t* comp_cnt;          // [B*Hkv] or null
   int32_t* comp_off;          // [B*Hkv + 1]
   int comp_chunk;
-  int recover;                // the attention kernel recovers rejected heads (page counts)
+  int decision_external;      // the decision may change before the attention kernel reads it
+                              // (phased steps): complement counts ignore the local reuse
 };
 cudaError_t launch_select_gate(const SelectParams& p, cudaStream_t s, bool pdl);
 

@@ -399,8 +399,61 @@ score_stream_kernel(const __grid_constant__ ScoreStreamArgs a) {
   // ================================ consumers ================================
   const int sub = lane % LPR, half = lane / LPR;
   const int G = a.hq / hkv;
+  // KV heads to consumer warps: with hkv >= 8, warp w takes heads w and w + 8
+  // of every page; with fewer heads (a rank of a head-sharded model holds one
+  // or two) the warps of head h take turns over the pages, so all of them work
+  const int wph = hkv >= kSSNC ? 1 : kSSNC / hkv;          // warps per head
+  const int h0 = hkv >= kSSNC ? warp : warp % hkv;
+  const int pslot = hkv >= kSSNC ? 0 : warp / hkv;         // my pages: j % wph == pslot
+  const bool has_head = hkv >= kSSNC || warp < hkv * wph;
   int cur_b = -1, ctx = 0;
   float qf[HPW][VN];
+  // q_rep slices of my heads for sequence b: mean of the group in fp32,
+  // rounded to q's dtype (page_scores.py:94-95)
+  auto load_qrep = [&](int b) {
+    cur_b = b;
+    ctx = a.lens[b];
+#pragma unroll
+    for (int e = 0; e < HPW; ++e) {
+      const int h = h0 + e * kSSNC;
+      if (h < hkv) {
+        float acc[VN];
+        const TQ* qb = reinterpret_cast<const TQ*>(a.q) + ((int64_t)b * a.hq + (int64_t)h * G) * D +
+                       sub * VN;
+        for (int g = 0; g < G; ++g) {
+          float t[VN];
+          load_q_slice<TQ, VN>(qb + (int64_t)g * D, t);
+#pragma unroll
+          for (int i = 0; i < VN; ++i) acc[i] = (g == 0) ? t[i] : acc[i] + t[i];
+        }
+        const float inv = 1.0f / (float)G;
+#pragma unroll
+        for (int i = 0; i < VN; ++i) qf[e][i] = Elem<TQ>::to_f(Elem<TQ>::from_f(acc[i] * inv));
+      }
+    }
+  };
+  if (n > 0) {
+    // the first sequence's q_rep is computed while the first pages are in
+    // flight (after they land its loads would queue behind the page stream);
+    // the q rows of the next two sequences are prefetched into L2
+    auto seq_of = [&](int x) -> int {
+      int lo = 0, hi = B - 1;  // largest b with bpref[b] <= x
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (bpref[mid] <= x) lo = mid;
+        else hi = mid - 1;
+      }
+      return lo;
+    };
+    const int b_first = seq_of(Xc), b_last = min(seq_of(Xe - 1), b_first + 2);
+    const int row_bytes = a.hq * D * (int)sizeof(TQ);
+    for (int b = b_first + 1; b <= b_last; ++b) {
+      const char* qrow = reinterpret_cast<const char*>(a.q) + (int64_t)b * row_bytes;
+      for (int off = (warp * 32 + lane) * 128; off < row_bytes; off += kSSNC * 32 * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(qrow + off));
+    }
+    load_qrep(b_first);
+  }
   for (int j = 0; j < n; ++j) {
     const int st = j % S;
     if (!mbar_wait_bounded(&full[st], (j / S) & 1)) {
@@ -411,35 +464,13 @@ score_stream_kernel(const __grid_constant__ ScoreStreamArgs a) {
     const int b = m.x;
     const bool ok = m.y >= 0;
     const int p = ok ? m.y : -1 - m.y;
-    if (b != cur_b) {
-      // q_rep slices of my heads: mean of the group in fp32, rounded to q's
-      // dtype (page_scores.py:94-95)
-      cur_b = b;
-      ctx = a.lens[b];
-#pragma unroll
-      for (int e = 0; e < HPW; ++e) {
-        const int h = warp + e * kSSNC;
-        if (h < hkv) {
-          float acc[VN];
-          const TQ* qb = reinterpret_cast<const TQ*>(a.q) + ((int64_t)b * a.hq + (int64_t)h * G) * D +
-                         sub * VN;
-          for (int g = 0; g < G; ++g) {
-            float t[VN];
-            load_q_slice<TQ, VN>(qb + (int64_t)g * D, t);
-#pragma unroll
-            for (int i = 0; i < VN; ++i) acc[i] = (g == 0) ? t[i] : acc[i] + t[i];
-          }
-          const float inv = 1.0f / (float)G;
-#pragma unroll
-          for (int i = 0; i < VN; ++i) qf[e][i] = Elem<TQ>::to_f(Elem<TQ>::from_f(acc[i] * inv));
-        }
-      }
-    }
+    if (b != cur_b) load_qrep(b);
     const int ntok = min(kBlk, ctx - p * kBlk);
+    const bool mine = has_head && (j % wph) == pslot;
 #pragma unroll
     for (int e = 0; e < HPW; ++e) {
-      const int h = warp + e * kSSNC;
-      if (h >= hkv) continue;
+      const int h = h0 + e * kSSNC;
+      if (!mine || h >= hkv) continue;
       float mx = neg_inf();
       if (ok) {
         const uint8_t* base = ring + (size_t)st * PB + ((size_t)h * D + sub * VN) * sizeof(T);

@@ -237,7 +237,7 @@ __device__ void finish_select(const SelectParams& p, int cta_rejects, int* s_fla
   if (!s_flag[0] || !p.comp_off) return;
   __threadfence();  // the other CTAs' comp_cnt
   const int heads = p.B * p.hkv;
-  const bool reuse = (p.mode == CVSA_MODE_LAZY) && s_flag[1];
+  const bool reuse = (p.mode == CVSA_MODE_LAZY) && s_flag[1] && !p.decision_external;
   int carry = 0;
   for (int base = 0; base < heads; base += NT) {
     const int i = base + threadIdx.x;

@@ -69,7 +69,7 @@ class StepConfig(ctypes.Structure):
 class StepIO(ctypes.Structure):
     _fields_ = [
         ("cached_indices", ctypes.c_void_p), ("cached_n", ctypes.c_void_p),
-        ("max_sel", ctypes.c_int32), ("reserved0", ctypes.c_int32),
+        ("max_sel", ctypes.c_int32), ("phase", ctypes.c_int32),
         ("out", ctypes.c_void_p), ("page_scores", ctypes.c_void_p),
         ("accept", ctypes.c_void_p), ("coverage", ctypes.c_void_p),
         ("counters", ctypes.c_void_p), ("step_flags", ctypes.c_void_p),
@@ -100,6 +100,7 @@ _SIGS = {
                           ctypes.POINTER(StepConfig), ctypes.POINTER(StepIO), _P, ctypes.c_size_t,
                           _P], ctypes.c_int),
     "cvsa_workspace_reset": ([_P, ctypes.c_size_t, _P], ctypes.c_int),
+    "cvsa_step_decision_word": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "cvsa_paged_append": ([ctypes.POINTER(KvDesc), _P, _P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _P,
                            _P], ctypes.c_int),
     "cvsa_paged_gather": ([ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P, _P], ctypes.c_int),
@@ -107,6 +108,9 @@ _SIGS = {
                                     _P, _P, _P, _P, _I, _P], ctypes.c_int),
 }
 NOALLOC_SCRATCH_BYTES = 8 << 20
+ABI_VERSION = 2
+# cvsa_decode_step phases (include/cvsa_b200.h CVSA_PHASE_*)
+PHASE_ALL, PHASE_SELECT, PHASE_ATTEND = 0, 1, 2
 
 _lib = None
 _lock = threading.Lock()
@@ -136,7 +140,7 @@ def load(path: Optional[str] = None) -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = res
-        if lib.cvsa_abi_version() != 1:
+        if lib.cvsa_abi_version() != ABI_VERSION:
             raise RuntimeError("libcvsa_b200.so ABI version mismatch")
         if path is None:
             _lib = lib

@@ -22,7 +22,13 @@ A layer without a cached selection takes a scoring step (the reference's
 _reuse_step re-enters __call__ with step - 1 for that case).
 
 Extensions (off by default): `sink_pages` / `local_pages` always-kept pages,
-and the stable (score desc, page index asc) top-k order. Options of the
+the stable (score desc, page index asc) top-k order, and `process_group`:
+the KV heads are sharded over the ranks of a torch.distributed group (one
+process per GPU; this rank holds `num_kv_heads` of them with their
+`num_q_heads` query heads), and the lazy step's batch-global decision is
+all-reduced (MIN of one int32) over the group between the selection and the
+attention kernels, so every rank reuses or re-selects together exactly as
+one GPU holding all heads would. Options of the
 reference that select pages differently (adaptive_selection,
 static_budget_table, selector='quest', top_p, light_normalizer), approximate
 recovery, the random-reject counterfactual and the decoupled coverage
@@ -59,6 +65,18 @@ class _LayerState:
                        if keep_scores else None)
 
 
+class StepHandle:
+    """A layer step in flight: `out` (final once `decision` is None) and, for
+    the selection half of a phased lazy step, the int32 device word holding
+    this rank's decision (bit0: every head of this rank accepted)."""
+    __slots__ = ("out", "decision", "args")
+
+    def __init__(self, out, decision, args):
+        self.out = out
+        self.decision = decision
+        self.args = args
+
+
 class CVSABackend:
     """CVSA backend: draft with sparse attention, verify with coverage, recover."""
 
@@ -87,6 +105,7 @@ class CVSABackend:
         sink_pages: int = 0,
         local_pages: int = 0,
         keep_page_scores: bool = False,
+        process_group=None,
     ):
         # argument checks of the reference (backend.py:150-178)
         if selector not in ("exact", "quest"):
@@ -144,9 +163,11 @@ class CVSABackend:
         self.sink_pages = sink_pages
         self.local_pages = local_pages
         self.keep_page_scores = keep_page_scores
+        self.process_group = process_group
+        self._decision_views: Dict[int, torch.Tensor] = {}  # workspace ptr -> int32 view
 
         self._layers: Dict[int, _LayerState] = {}
-        self._ws: Dict[int, tuple] = {}                  # stream -> (ptr, bytes, tensor)
+        self._ws: Dict[tuple, tuple] = {}  # (stream, private) -> (ptr, bytes, tensor)
         self._counters: Optional[torch.Tensor] = None   # int64[8] device
         self._dev_error: Optional[torch.Tensor] = None
         self._step = 0
@@ -278,6 +299,21 @@ class CVSABackend:
     def __call__(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                  block_tables: torch.Tensor, context_lens: torch.Tensor,
                  layer_idx: int) -> torch.Tensor:
+        h = self.begin_step(q, k_cache, v_cache, block_tables, context_lens, layer_idx,
+                            phased=self.process_group is not None)
+        if h.decision is not None:
+            exchange_decision(h.decision, self.process_group)
+            self.finish_step(h)
+        return h.out
+
+    def begin_step(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                   block_tables: torch.Tensor, context_lens: torch.Tensor, layer_idx: int,
+                   phased: bool = False) -> "StepHandle":
+        """Enqueue a layer step. With `phased` a lazy check step stops after
+        the selection: the handle's `decision` is the device word to combine
+        over the ranks holding the other KV heads (MIN), and finish_step runs
+        the attention. Other steps (and phased=False) run whole; their handle
+        has decision None and `out` is final."""
         self._last_accept_mask.pop(layer_idx, None)
         self._last_expanded_selection.pop(layer_idx, None)
         if q.dim() == 4:
@@ -323,7 +359,7 @@ class CVSABackend:
         io.timing_events = None
         cfg.mode = mode
         cfg.has_cache = 1 if st.has_cache else 0
-        ws = self._workspace(st.ws_bytes, dev, stream)
+        ws = self._workspace(st.ws_bytes, dev, stream, private=phased)
         events = None
         if self._timing_events is not None:
             io.timing_events = ctypes.cast(self._timing_events, ctypes.c_void_p)
@@ -333,23 +369,72 @@ class CVSABackend:
                 e.record()      # torch creates the cudaEvent_t at its first record
             arr = (ctypes.c_void_p * _lib.NUM_EVENTS)(*[e.cuda_event for e in events])
             io.timing_events = ctypes.cast(arr, ctypes.c_void_p)
-        rc = lib.cvsa_decode_step(qd, kvd, cfg, io, ws[0], ws[1], stream)
-        if rc:
-            _lib.check(rc, "cvsa_decode_step")
+        # the handle holds every tensor the descriptors point at (q and the
+        # tables may be fresh contiguous copies): the attention half of a
+        # phased step runs after this call returns, and a tensor freed here
+        # could be handed to work enqueued before it
+        handle = StepHandle(out, None, (qd, kvd, cfg, io, ws, stream, out.data_ptr(),
+                                        (q, bt, cl, k_cache, v_cache)))
+        if phased and mode == _lib.MODE_LAZY:
+            # heads sharded over ranks: the lazy decision is exchanged between
+            # the selection and the attention halves of the step
+            io.phase = _lib.PHASE_SELECT
+            rc = lib.cvsa_decode_step(qd, kvd, cfg, io, ws[0], ws[1], stream)
+            io.phase = _lib.PHASE_ALL
+            if rc:
+                _lib.check(rc, "cvsa_decode_step (select)")
+            handle.decision = self._decision_view(ws)
+        else:
+            rc = lib.cvsa_decode_step(qd, kvd, cfg, io, ws[0], ws[1], stream)
+            if rc:
+                _lib.check(rc, "cvsa_decode_step")
         if events is not None:
             self._pending_events.append((mode, events))
         if mode in (_lib.MODE_SCORE, _lib.MODE_LAZY):
             st.has_cache = True
             self._last_accept_mask[layer_idx] = st.accept_bool
-        return out
+        return handle
 
-    def _workspace(self, nbytes: int, dev: torch.device, stream: int):
-        """(pointer, bytes) of a zeroed 256-aligned workspace for this stream."""
-        ws = self._ws.get(stream)
+    def finish_step(self, h: "StepHandle") -> torch.Tensor:
+        """Run the attention half of a phased step (after its decision word
+        holds the combined decision); returns the step's output."""
+        if h.decision is None:
+            return h.out
+        qd, kvd, cfg, io, ws, stream, out_ptr, _alive = h.args
+        io.phase = _lib.PHASE_ATTEND
+        io.out = out_ptr
+        rc = _lib.load().cvsa_decode_step(qd, kvd, cfg, io, ws[0], ws[1], stream)
+        io.phase = _lib.PHASE_ALL
+        if rc:
+            _lib.check(rc, "cvsa_decode_step (attend)")
+        h.decision = None
+        h.args = None
+        return h.out
+
+    def _decision_view(self, ws) -> torch.Tensor:
+        """int32 view of the workspace's lazy-decision word (cvsa_step_decision_word)."""
+        view = self._decision_views.get(ws[0])
+        if view is None:
+            word = ctypes.c_void_p()
+            _lib.check(_lib.load().cvsa_step_decision_word(ws[0], ctypes.byref(word)),
+                       "cvsa_step_decision_word")
+            off = word.value - ws[0]
+            view = ws[2][off:off + 4].view(torch.int32)
+            self._decision_views[ws[0]] = view
+        return view
+
+    def _workspace(self, nbytes: int, dev: torch.device, stream: int, private: bool = False):
+        """(pointer, bytes, tensor) of a zeroed 256-aligned workspace for this
+        stream. Whole steps run one after another in stream order, so backends
+        share one; a phased step keeps its selection in the workspace until its
+        attention half, so it takes one of its own."""
+        key = (stream, private)
+        ws = self._ws.get(key)
         if ws is None or ws[1] < nbytes:
-            buf = _lib.WORKSPACE.get(nbytes, dev, f"step-{stream}")
+            tag = f"step-{stream}" + (f"-{id(self)}" if private else "")
+            buf = _lib.WORKSPACE.get(nbytes, dev, tag)
             ws = (buf.data_ptr(), buf.numel(), buf)
-            self._ws[stream] = ws
+            self._ws[key] = ws
         return ws
 
     # ---- tracing helpers -------------------------------------------------
@@ -364,3 +449,23 @@ class CVSABackend:
         """Device word: bit0 every head accepted, bit1 the selection was rescored."""
         st = self._layers.get(layer_idx)
         return None if st is None else st.flags
+
+
+def exchange_decision(decision: torch.Tensor, group) -> torch.Tensor:
+    """All-reduce the lazy decision word over `group` (MIN: bit0 stays set only
+    if every rank's heads all accepted their cached selection), in place, in
+    stream order. backend.py:446 takes `accept_mask.all()` over every head of
+    the batch; with the heads sharded over ranks that is this reduction."""
+    import torch.distributed as dist
+    dist.all_reduce(decision, op=dist.ReduceOp.MIN, group=group)
+    return decision
+
+
+def shard_heads(num_kv_heads: int, num_q_heads: int, rank: int, world: int) -> Tuple[slice, slice]:
+    """KV heads and query heads rank `rank` of `world` holds: contiguous equal
+    blocks, query heads following their KV heads (GQA groups stay whole)."""
+    if num_kv_heads % world or num_q_heads % num_kv_heads:
+        raise ValueError(f"{num_kv_heads} KV heads do not shard over {world} ranks")
+    per = num_kv_heads // world
+    g = num_q_heads // num_kv_heads
+    return slice(rank * per, (rank + 1) * per), slice(rank * per * g, (rank + 1) * per * g)

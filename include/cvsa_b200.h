@@ -38,7 +38,7 @@
 extern "C" {
 #endif
 
-#define CVSA_ABI_VERSION 1
+#define CVSA_ABI_VERSION 2
 
 /* element types */
 enum {
@@ -233,7 +233,8 @@ typedef struct cvsa_step_io {
   int32_t* cached_indices; /* [batch, num_kv_heads, max_sel] in/out (_cached_selection) */
   int32_t* cached_n;       /* [batch, num_kv_heads] in/out */
   int32_t max_sel;         /* >= budget + sink_pages + local_pages */
-  int32_t reserved0;
+  int32_t phase;           /* CVSA_PHASE_*: the whole step, or its two halves around
+                              an exchange of the lazy decision between ranks */
   void* out;               /* [batch, num_q_heads, head_dim], q dtype */
   float* page_scores;      /* [batch, num_kv_heads, max_pages] out, or NULL */
   uint8_t* accept;         /* [batch, num_kv_heads] gate of the selection decoded, or NULL */
@@ -249,6 +250,19 @@ typedef struct cvsa_step_io {
    * leave their pair unrecorded. Timing disables launch overlap (PDL). */
   void* const* timing_events;
 } cvsa_step_io_t;
+
+/* Phases of cvsa_decode_step. A step whose KV heads are sharded over ranks
+ * (one process per GPU, each holding some KV heads of every sequence) needs
+ * the lazy decision of backend.py:446 (accept_mask.all()) over all heads:
+ * run CVSA_PHASE_SELECT, all-reduce the word at cvsa_step_decision_word with
+ * MIN over the ranks (bit0: every cached head accepted), then run
+ * CVSA_PHASE_ATTEND with the same arguments and workspace. The step
+ * statistics of the selection count the rank's own decision. */
+enum {
+  CVSA_PHASE_ALL = 0,     /* scoring, selection and attention */
+  CVSA_PHASE_SELECT = 1,  /* scoring and selection (LAZY / SCORE modes) */
+  CVSA_PHASE_ATTEND = 2   /* attention, after CVSA_PHASE_SELECT */
+};
 
 enum {
   CVSA_EV_SCORE_BEGIN = 0, CVSA_EV_SCORE_END = 1,
@@ -271,6 +285,10 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
 
 /* Zero a workspace (cudaMemsetAsync). */
 int cvsa_workspace_reset(void* workspace, size_t workspace_bytes, void* stream);
+
+/* The device word (int32) of a step workspace that holds the lazy decision
+ * between CVSA_PHASE_SELECT and CVSA_PHASE_ATTEND (backend.py:446). */
+int cvsa_step_decision_word(void* workspace, int32_t** word);
 
 /* ---- paged KV runtime (cvsa/runtime/kv_cache.py) -------------------- */
 

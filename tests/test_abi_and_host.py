@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_status_strings():
     lib = _lib.load()
-    assert lib.cvsa_abi_version() == 1
+    assert lib.cvsa_abi_version() == _lib.ABI_VERSION == 2
     assert lib.cvsa_status_string(0) == b"ok"
     assert lib.cvsa_status_string(-5) == b"page pool exhausted"
 
