@@ -311,6 +311,124 @@ def measure_config3(dev, steps, warmup, ws):
             "per_head_accept_rate": stats.get("per_head_accept_rate")}
 
 
+C4_LAYERS = 80
+C4_POOLS = 16
+
+
+def measure_config4(dev, steps, warmup, ws, rank):
+    """Config 4 (Llama-70B attention: B=8, Hq=64, Hkv=8, D=128, ctx 32768, 80
+    layers), KV heads sharded over the ranks: rank r holds KV heads
+    [8r/N, 8(r+1)/N) and their query heads, and the lazy check step all-reduces
+    the batch-global decision (one int32, MIN, NCCL) between its selection and
+    attention halves. Layer l reads pool l % C4_POOLS (each pool 1.07 GB / N of
+    K+V, so consecutive uses of a pool are 15 pools apart, far beyond L2). The
+    lazy-check and reuse steps are captured as CUDA graphs (the all-reduce
+    inside) and timed separately; times are the max over ranks."""
+    from cvsa import _lib, synthetic
+    from cvsa.backend import CVSABackend, shard_heads
+
+    kv_s, q_s = shard_heads(8, 64, rank, ws)
+    pools = [synthetic.config4(device=dev, kv_heads=kv_s, seed=4000 + i)
+             for i in range(C4_POOLS)]
+    torch.cuda.synchronize()
+    B, Hq, D = pools[0].q.shape
+    hkv = pools[0].num_kv_heads
+    pg = None
+    if ws > 1:
+        import torch.distributed as dist
+        pg = dist.group.WORLD
+    be = CVSABackend(hkv, Hq, D, 16, num_layers=C4_LAYERS, budget_pct=0.05,
+                     coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
+                     sink_pages=1, local_pages=2, process_group=pg)
+
+    def step():
+        for l in range(C4_LAYERS):
+            wl = pools[l % C4_POOLS]
+            be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+            be.step_done(l, C4_LAYERS)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs, launch = {}, "CUDA graph per step kind (NCCL all-reduce inside the lazy-check graph)"
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, M_INTERVAL)):
+            step()
+        side.synchronize()
+        ok = 1
+        try:
+            for kind, step_idx in (("lazy", 0), ("reuse", 1)):
+                g = torch.cuda.CUDAGraph()
+                be._step = step_idx
+                with torch.cuda.graph(g, stream=side):
+                    for l in range(C4_LAYERS):
+                        wl = pools[l % C4_POOLS]
+                        be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+                graphs[kind] = g
+        except Exception:  # noqa: BLE001 - capture unsupported here: time eager steps
+            ok = 0
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    if ws > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = int(t.item())
+    if not ok:
+        graphs = {}
+        launch = "eager (graph capture of the collective failed)"
+
+    def run(kind, n):
+        be._step = 0 if kind == "lazy" else 1
+        if graphs:
+            graphs[kind].replay()
+            for _ in range(n - 1):
+                graphs[kind].replay()
+        else:
+            for _ in range(n):
+                be._step = 0 if kind == "lazy" else 1
+                for l in range(C4_LAYERS):
+                    wl = pools[l % C4_POOLS]
+                    be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
+
+    res = {}
+    n = max(steps // 2, 2)
+    for kind in ("lazy", "reuse"):
+        run(kind, 1)
+        torch.cuda.synchronize()
+        _barrier(ws)
+        c0 = be._counter_values()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run(kind, n)
+        e1.record()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        ms = _max_over_ranks(e0.elapsed_time(e1), ws)
+        c1 = be._counter_values()
+        pages = c1[_lib.CTR_PAGES_ATTENDED] - c0[_lib.CTR_PAGES_ATTENDED]
+        scoring = (n * C4_LAYERS * _scoring_pages(pools[0].context_lens, hkv) * KP_BYTES
+                   if kind == "lazy" else 0)
+        per_rank_bytes = float(pages * 2 * KP_BYTES + scoring)
+        res[kind] = (ms * 1e3 / (n * C4_LAYERS), _sum_over_ranks(per_rank_bytes, ws) / (ms * 1e-3) / 1e9)
+    stats = be.get_stats()
+    del graphs
+    us_layer = (res["lazy"][0] + (M_INTERVAL - 1) * res["reuse"][0]) / M_INTERVAL
+    step_s = us_layer * C4_LAYERS * 1e-6
+    gbs = (res["lazy"][1] * res["lazy"][0] + (M_INTERVAL - 1) * res["reuse"][1] * res["reuse"][0]) / (
+        M_INTERVAL * us_layer)
+    return {"workload": "config4: Llama-70B attention, B=8, Hq=64, Hkv=8, D=128, bf16, ctx=32768 "
+                        "(2048 pages), budget 5% (102) + sink 1 + local 2, tau=0.9, lazy M=4, "
+                        f"{C4_LAYERS} layers over {C4_POOLS} rotating pools",
+            "parallelism": f"KV heads sharded over {ws} GPU(s): {hkv} KV + {Hq} query heads each",
+            "launch": launch,
+            "us_per_layer_lazy_check": res["lazy"][0], "us_per_layer_reuse": res["reuse"][0],
+            "us_per_layer": us_layer, "tokens_per_s": B / step_s,
+            "value": gbs, "unit": "GB/s (all GPUs, algorithmic KV bytes)",
+            "frac_of_peak": gbs / (_peaks()[0] * ws),
+            "per_head_accept_rate_rank0": stats.get("per_head_accept_rate")}
+
+
 def run_cvsa(args, ws, rank, local):
     import ctypes
 
@@ -485,6 +603,9 @@ def run_cvsa(args, ws, rank, local):
     if not args.no_c3:
         c3 = measure_config3(dev, args.steps, warm, ws)
         c3["frac_of_peak"] = c3["value"] / (_peaks()[0] * ws)
+    c4 = None
+    if not args.no_c4:
+        c4 = measure_config4(dev, args.steps, warm, ws, rank)
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
@@ -540,6 +661,8 @@ def run_cvsa(args, ws, rank, local):
         }
         if c3 is not None:
             line["config3_128k"] = c3
+        if c4 is not None:
+            line["config4_70b_head_sharded"] = c4
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -554,6 +677,8 @@ def main():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
     ap.add_argument("--no-c3", action="store_true", help="skip the config-3 (128K) measurement")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="skip the config-4 (70B, KV heads sharded over the GPUs) measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

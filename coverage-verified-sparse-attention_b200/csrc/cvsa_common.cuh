@@ -175,7 +175,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 3-D tiled TMA load (no multicast) into this CTA's shared memory, completing
+// 3-D tiled TMA load (this CTA only) into this CTA's shared memory, completing
 // on `bar` with complete_tx. Coordinates are element indices (x innermost).
 __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int x, int y, int z) {
@@ -187,7 +187,7 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
-// 4-D tiled TMA load (no multicast); coordinates innermost first.
+// 4-D tiled TMA load (this CTA only); coordinates innermost first.
 __device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map,
                                             uint64_t* bar, int x, int y, int z, int w) {
   asm volatile(
@@ -229,8 +229,9 @@ __device__ __forceinline__ void cp_async_wait_dyn(int n) {
 }
 
 // Bulk (untiled) global -> shared copy of `bytes` (multiple of 16, both
-// addresses 16-byte aligned) completing on `bar` with complete_tx; no
-// multicast. `policy` is an L2 cache policy (make_evict_first_policy).
+// addresses 16-byte aligned) completing on `bar` with complete_tx, into this
+// CTA's own shared memory. `policy` is an L2 cache policy
+// (make_evict_first_policy).
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes,
                                           uint64_t* bar, uint64_t policy) {
   asm volatile(
