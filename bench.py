@@ -429,6 +429,102 @@ def measure_config4(dev, steps, warmup, ws, rank):
             "per_head_accept_rate_rank0": stats.get("per_head_accept_rate")}
 
 
+C5_STEPS = 256
+
+
+def measure_config5(dev, warmup, ws, rank):
+    """Config 5: 64 ragged sequences (1K-64K tokens) in a pool with a shuffled
+    free list; every step appends one token per sequence (cvsa_paged_append,
+    new pages taken on the device) and runs one lazy-M=4 layer step. Nearly
+    every head fails tau, so scoring steps recover almost every page. The
+    append, the lazy-check step and the reuse step are captured as CUDA graphs;
+    C5_STEPS steps are timed (max over ranks; each rank its own batch), and
+    the appends alone separately."""
+    from cvsa import _lib, synthetic
+    from cvsa.backend import CVSABackend
+
+    grow = C5_STEPS + 3 * M_INTERVAL + 16
+    wl = synthetic.config5(device=dev, seed=5000 + rank, grow=grow)
+    mgr, cache = wl.mgr, wl.cache
+    B, Hq, D = wl.q.shape
+    hkv = cache.num_kv_heads
+    be = CVSABackend(hkv, Hq, D, 16, num_layers=1, budget_pct=wl.budget_pct,
+                     coverage_threshold=wl.tau, lazy=True, check_interval=M_INTERVAL,
+                     sink_pages=wl.sink_pages, local_pages=wl.local_pages)
+
+    def decode():
+        be(wl.q, cache.k_cache, cache.v_cache, mgr.block_tables, mgr.context_lens, 0)
+
+    def append():
+        mgr.append_batch(wl.k_new, wl.v_new)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs = {}
+    with torch.cuda.stream(side):
+        for _ in range(M_INTERVAL):              # one eager cycle (the first step scores)
+            append()
+            decode()
+            be.step_done(0, 1)
+        side.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            append()
+        graphs["append"] = g
+        for kind, step_idx in (("lazy", 0), ("reuse", 1)):
+            g = torch.cuda.CUDAGraph()
+            be._step = step_idx
+            with torch.cuda.graph(g, stream=side):
+                decode()
+            graphs[kind] = g
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize()
+    lens0 = mgr.context_lens.to(torch.int64).cpu()   # before the timed steps
+
+    def run(n, with_decode=True):
+        for s in range(n):
+            graphs["append"].replay()
+            if with_decode:
+                graphs["lazy" if s % M_INTERVAL == 0 else "reuse"].replay()
+
+    _barrier(ws)
+    torch.cuda.synchronize()
+    c0 = be._counter_values()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    run(C5_STEPS)
+    e1.record()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    ms = _max_over_ranks(e0.elapsed_time(e1), ws)
+    c1 = be._counter_values()
+    pages = c1[_lib.CTR_PAGES_ATTENDED] - c0[_lib.CTR_PAGES_ATTENDED]
+    scoring = sum(int(((lens0 + s + 1 + 15) // 16).sum()) * hkv * KP_BYTES
+                  for s in range(C5_STEPS) if s % M_INTERVAL == 0)
+    nbytes = _sum_over_ranks(float(pages * 2 * KP_BYTES + scoring), ws)
+    a0 = torch.cuda.Event(enable_timing=True)
+    a1 = torch.cuda.Event(enable_timing=True)
+    n_app = 16
+    a0.record()
+    run(n_app, with_decode=False)
+    a1.record()
+    torch.cuda.synchronize()
+    app_us = _max_over_ranks(a0.elapsed_time(a1), ws) * 1e3 / n_app
+    cache.check()
+    stats = be.get_stats()
+    del graphs
+    return {"workload": f"config5: {B} ragged sequences, lengths U[1024, 65536] (+1 token per "
+                        "step), Hq=32, Hkv=8, D=128, bf16, shuffled free list, budget 5% of the "
+                        f"table width + sink 1 + local 2, tau=0.9, lazy M=4, {C5_STEPS} steps of "
+                        "append + one layer",
+            "value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s (algorithmic KV bytes)",
+            "us_per_step": ms * 1e3 / C5_STEPS, "append_us": app_us,
+            "frac_of_peak": nbytes / (ms * 1e-3) / 1e9 / (_peaks()[0] * ws),
+            "per_head_accept_rate": stats.get("per_head_accept_rate"),
+            "launch": "CUDA graphs: append, lazy-check step, reuse step"}
+
+
 def run_cvsa(args, ws, rank, local):
     import ctypes
 
@@ -606,6 +702,9 @@ def run_cvsa(args, ws, rank, local):
     c4 = None
     if not args.no_c4:
         c4 = measure_config4(dev, args.steps, warm, ws, rank)
+    c5 = None
+    if not args.no_c5:
+        c5 = measure_config5(dev, warm, ws, rank)
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
@@ -663,6 +762,8 @@ def run_cvsa(args, ws, rank, local):
             line["config3_128k"] = c3
         if c4 is not None:
             line["config4_70b_head_sharded"] = c4
+        if c5 is not None:
+            line["config5_ragged_append"] = c5
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
@@ -679,6 +780,8 @@ def main():
     ap.add_argument("--no-c3", action="store_true", help="skip the config-3 (128K) measurement")
     ap.add_argument("--no-c4", action="store_true",
                     help="skip the config-4 (70B, KV heads sharded over the GPUs) measurement")
+    ap.add_argument("--no-c5", action="store_true",
+                    help="skip the config-5 (ragged batch with appends) measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

@@ -1,0 +1,309 @@
+"""Page-split CVSA step: each rank holds a contiguous range of every
+sequence's pages (one long sequence spread over GPUs, config 3 across ranks).
+
+The reference has no multi-GPU path; this follows its single-GPU semantics
+(cvsa/backend.py:683-864 scoring step, :392-465 lazy step, :866-881 reuse)
+with the selection, the attention partials and the coverage sums combined
+over the ranks:
+
+  1. every rank scores its pages and proposes its best `budget` non-forced
+     pages (score, global page index); an all-gather of the proposals lets
+     every rank take the same global top-`budget` (score descending, page
+     ascending; proposals are concatenated in rank order, so table position
+     order is page order). Forced pages: the sink pages live on rank 0, the
+     local pages on the last rank;
+  2. every rank attends its share of the selection (unnormalised partial
+     (o, m, l)) and sums its pages' log-sum-exp terms (all valid pages, and
+     the selected ones); an all-gather of both lets every rank merge them in
+     fixed rank order: the draft output, coverage exp(lse_sel - lse_all) and
+     the accept mask (coverage.py:160-215) are identical on every rank;
+  3. if a head rejects, exact recovery: every rank attends all its valid
+     pages of the rejected heads (draft and complement partition them, so
+     this is the merged result of backend.py:818-844) and a third all-gather
+     merges them.
+Reuse steps need only exchange 2 (partials). A lazy check step gathers the
+cached selection's coverage sums first and continues as a reuse or a scoring
+step on every rank alike.
+
+A step is a generator that yields each 1-D float32 tensor to all-gather and
+receives the [world, n] result; `run_step` drives it with torch.distributed,
+and tests can drive the ranks of one process in lockstep.
+"""
+
+from typing import Callable, Dict, List, Optional, Tuple
+
+import torch
+
+from cvsa.kernels.select import budget_for
+
+NEG_INF = float("-inf")
+
+
+def page_range(n_pages: torch.Tensor, rank: int, world: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[lo, hi) of each sequence's pages held by `rank`: contiguous, sizes differ by <= 1."""
+    n = n_pages.to(torch.int64)
+    return n * rank // world, n * (rank + 1) // world
+
+
+def shard_sequence(k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                   context_lens: torch.Tensor, rank: int, world: int, block_size: int):
+    """This rank's part of a paged batch: a pool holding only its pages, its
+    block tables (local page p = global page lo + p) and local context lengths
+    (tokens inside its range; the last rank keeps the partial last page)."""
+    ctx = context_lens.to(torch.int64).cpu()
+    nv = (ctx + block_size - 1) // block_size
+    lo, hi = page_range(nv, rank, world)
+    B = block_tables.shape[0]
+    W = int((hi - lo).max()) if B else 0
+    bt_cpu = block_tables.cpu()
+    blocks = []
+    table = torch.zeros((B, max(W, 1)), dtype=torch.int32)
+    for b in range(B):
+        ids = bt_cpu[b, int(lo[b]):int(hi[b])].long()
+        table[b, :ids.numel()] = torch.arange(len(blocks), len(blocks) + ids.numel(),
+                                              dtype=torch.int32)
+        blocks.extend(ids.tolist())
+    idx = torch.tensor(blocks, dtype=torch.long, device=k_cache.device)
+    k_local = k_cache.index_select(0, idx).contiguous()
+    v_local = v_cache.index_select(0, idx).contiguous()
+    cl_local = (torch.minimum(hi * block_size, ctx) - lo * block_size).clamp(min=0)
+    return (k_local, v_local, table.to(k_cache.device),
+            cl_local.to(torch.int32).to(k_cache.device))
+
+
+class DeviceOps:
+    """The kernels of a page-split step: this package's CUDA ops."""
+
+    def __init__(self):
+        from cvsa.kernels import page_scores, select, sparse_decode
+        self.score_pages = page_scores.score_pages
+        self.select_pages = select.select_pages
+        self.decode_unnorm = sparse_decode.sparse_decode_unnorm
+
+
+def run_step(gen, allgather: Callable[[torch.Tensor], torch.Tensor]):
+    """Drive a step generator: each yielded 1-D tensor is all-gathered."""
+    try:
+        x = next(gen)
+        while True:
+            x = gen.send(allgather(x))
+    except StopIteration as e:
+        return e.value
+
+
+def dist_allgather(group=None) -> Callable[[torch.Tensor], torch.Tensor]:
+    import torch.distributed as dist
+
+    def ag(x: torch.Tensor) -> torch.Tensor:
+        world = dist.get_world_size(group)
+        outs = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(outs, x.contiguous(), group=group)
+        return torch.stack(outs)
+    return ag
+
+
+def _pack(*ts: torch.Tensor) -> torch.Tensor:
+    return torch.cat([t.reshape(-1).to(torch.float32) for t in ts])
+
+
+def _unpack(flat: torch.Tensor, *shapes) -> List[torch.Tensor]:
+    out, off = [], 0
+    for s in shapes:
+        n = 1
+        for d in s:
+            n *= d
+        out.append(flat[..., off:off + n].reshape(flat.shape[:-1] + tuple(s)))
+        off += n
+    return out
+
+
+def _compact(mask: torch.Tensor, values: torch.Tensor, width: int, fill):
+    """Entries of `values` where `mask`, in order, left-aligned in `width` slots."""
+    order = torch.argsort((~mask).to(torch.int8), dim=-1, stable=True)
+    v = torch.gather(values, -1, order)[..., :width]
+    m = torch.gather(mask, -1, order)[..., :width]
+    return torch.where(m, v, torch.full_like(v, fill)), m.sum(-1).to(torch.int32)
+
+
+def _merge_partials(o, m, l):
+    """Fixed-order merge over ranks (dim 0) of unnormalised (o, m, l) partials."""
+    M = m.amax(0)
+    w = torch.where(torch.isinf(m) & (m < 0), torch.zeros_like(m),
+                    torch.exp(m - torch.where(torch.isinf(M), torch.zeros_like(M), M)))
+    return (o * w.unsqueeze(-1)).sum(0), M, (l * w).sum(0)
+
+
+class PageSplitBackend:
+    """CVSA step over the pages a rank holds (see the module docstring).
+
+    Called like CVSABackend with this rank's pool, block tables and local
+    context lengths (shard_sequence), plus the global context lengths and the
+    global block-table width (the budget is int(W * budget_pct), backend.py:690).
+    """
+
+    def __init__(self, num_kv_heads: int, num_q_heads: int, head_dim: int, block_size: int,
+                 rank: int, world: int, num_layers: int = 32, budget_pct: float = 0.10,
+                 reuse_interval: int = 16, coverage_threshold: float = 0.90, lazy: bool = False,
+                 check_interval: Optional[int] = None, sink_pages: int = 0, local_pages: int = 0,
+                 process_group=None, ops=None):
+        self.num_kv_heads = num_kv_heads
+        self.num_q_heads = num_q_heads
+        self.G = num_q_heads // num_kv_heads
+        self.head_dim = head_dim
+        self.block_size = block_size
+        self.rank, self.world = rank, world
+        self.num_layers = num_layers
+        self.budget_pct = budget_pct
+        self.reuse_interval = reuse_interval
+        self.tau = coverage_threshold
+        self.lazy = lazy
+        self.check_interval = check_interval or 1
+        self.sink_pages, self.local_pages = sink_pages, local_pages
+        self.process_group = process_group
+        self.ops = ops or DeviceOps()
+        self._cached: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+        self._step = 0
+        self.stats = dict(scoring_steps=0, coverage_checks=0, accept_steps=0, reject_steps=0,
+                          heads_accepted=0, heads_total=0)
+
+    def step_done(self, layer_idx: int, num_layers: int):
+        if layer_idx == num_layers - 1:
+            self._step += 1
+
+    def cached_selection(self, layer_idx: int):
+        """(local page indices [B, H_kv, max_sel] ascending, counts) of a layer."""
+        return self._cached.get(layer_idx)
+
+    def __call__(self, q, k_cache, v_cache, block_tables, context_lens, layer_idx,
+                 global_context_lens, global_table_width):
+        gen = self.step(q, k_cache, v_cache, block_tables, context_lens, layer_idx,
+                        global_context_lens, global_table_width)
+        return run_step(gen, dist_allgather(self.process_group))
+
+    # ---- the step ---------------------------------------------------------
+    def step(self, q, k, v, bt, cl, layer_idx, ctx_g, W_g):
+        """Generator: yields tensors to all-gather, returns the output [B, Hq, D]."""
+        B, Hq, D = q.shape
+        H, G, bs = self.num_kv_heads, self.G, self.block_size
+        r, N = self.rank, self.world
+        dev = q.device
+        budget = budget_for(int(W_g), self.budget_pct)
+        sink_r = self.sink_pages if r == 0 else 0
+        local_r = self.local_pages if r == N - 1 else 0
+        max_sel = budget + self.sink_pages + self.local_pages
+        nv_g = (ctx_g.to(torch.int64).to(dev) + bs - 1) // bs
+        lo, hi = page_range(nv_g, r, N)
+        nv_r = hi - lo                                          # [B]
+        if B and int((nv_g // N).min()) < self.sink_pages + self.local_pages:
+            raise ValueError("every rank needs at least sink_pages + local_pages pages "
+                             "of every sequence")
+        cached = self._cached.get(layer_idx)
+        if self.lazy:
+            check = self._step % self.check_interval == 0 or cached is None
+        else:
+            check = False
+        scoring = (self._step % self.reuse_interval == 0 or cached is None) if not self.lazy \
+            else check
+
+        def attend(idx, n):
+            return self.ops.decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs)
+
+        def lse_sums(scores, idx, n):
+            s_all = torch.logsumexp(scores, -1)
+            K = idx.shape[-1]
+            mask = torch.arange(K, device=dev).view(1, 1, K) < n.unsqueeze(-1)
+            sel = torch.gather(scores, -1, idx.long().clamp(min=0))
+            sel = torch.where(mask, sel, torch.full_like(sel, NEG_INF))
+            return s_all, torch.logsumexp(sel, -1)
+
+        def coverage(parts_all, parts_sel):
+            lse_all = torch.logsumexp(parts_all, 0)
+            lse_sel = torch.logsumexp(parts_sel, 0)
+            return torch.exp(lse_sel - lse_all)
+
+        def draft_output(idx, n, extra=()):
+            o, m, l = attend(idx, n)
+            got = yield _pack(o, m, l, *extra)
+            parts = _unpack(got, (B, Hq, D), (B, Hq), (B, Hq), *[tuple(t.shape) for t in extra])
+            O, M, L = _merge_partials(parts[0], parts[1], parts[2])
+            return O, L, parts[3:]
+
+        if not scoring and not check:                           # reuse step
+            idx, n = cached
+            O, L, _ = yield from draft_output(idx, n)
+            return (O / L.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
+
+        scores = self.ops.score_pages(q, k, bt, cl, H, G, bs).float()   # [B, H, W_r]
+        if check:
+            # lazy accounting of backend.py:420-465: every check counts; a layer
+            # without a cached selection counts as a reject
+            self.stats["coverage_checks"] += 1
+        if check and cached is None:
+            self.stats["reject_steps"] += 1
+        if check and cached is not None:
+            sa, ss = lse_sums(scores, *cached)
+            got = yield _pack(sa, ss)
+            pa, ps = _unpack(got, (B, H), (B, H))
+            acc = coverage(pa, ps) >= torch.tensor(self.tau, dtype=torch.float32)
+            self.stats["heads_accepted"] += int(acc.sum())
+            self.stats["heads_total"] += acc.numel()
+            if bool(acc.all()):
+                self.stats["accept_steps"] += 1
+                idx, n = cached
+                O, L, _ = yield from draft_output(idx, n)
+                return (O / L.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
+            self.stats["reject_steps"] += 1
+
+        # ---- scoring step ----
+        self.stats["scoring_steps"] += 1
+        idx_l, n_l = self.ops.select_pages(scores, cl, bs, budget, sink_r, local_r)
+        K = idx_l.shape[-1]
+        pos = torch.arange(K, device=dev).view(1, 1, K)
+        valid = pos < n_l.unsqueeze(-1)
+        il = idx_l.long()
+        forced = (il < sink_r) | (il >= (nv_r.view(B, 1, 1) - local_r))
+        cand = valid & ~forced
+        cand_s = torch.where(cand, torch.gather(scores, -1, il.clamp(min=0)),
+                             torch.full(il.shape, NEG_INF, device=dev))
+        cand_g = (il + lo.view(B, 1, 1)).to(torch.float32)
+        cs, _ = _compact(cand, cand_s, budget, NEG_INF)
+        cg, _ = _compact(cand, cand_g, budget, -1.0)
+        got = yield _pack(cs, cg)                               # [N, 2 * B * H * budget]
+        all_s, all_g = _unpack(got, (B, H, budget), (B, H, budget))
+        tab_s = all_s.permute(1, 2, 0, 3).reshape(B, H, N * budget).contiguous()
+        tab_g = all_g.permute(1, 2, 0, 3).reshape(B, H, N * budget)
+        tab_len = torch.full((B,), N * budget * bs, dtype=torch.int32, device=dev)
+        tpos, tn = self.ops.select_pages(tab_s, tab_len, bs, budget, 0, 0)
+        tm = torch.arange(tpos.shape[-1], device=dev).view(1, 1, -1) < tn.unsqueeze(-1)
+        sel_g = torch.gather(tab_g, -1, tpos.long().clamp(min=0))
+        sel_g = torch.where(tm & torch.isfinite(torch.gather(tab_s, -1, tpos.long().clamp(min=0))),
+                            sel_g, torch.full_like(sel_g, -1.0)).long()
+        # my pages of the global selection, with my forced pages, ascending
+        mine = (sel_g >= lo.view(B, 1, 1)) & (sel_g < hi.view(B, 1, 1))
+        loc = sel_g - lo.view(B, 1, 1)
+        sink_idx = torch.arange(sink_r, device=dev).view(1, 1, -1).expand(B, H, sink_r)
+        tail = (nv_r.view(B, 1, 1) - local_r + torch.arange(local_r, device=dev).view(1, 1, -1)
+                ).expand(B, H, local_r)
+        all_idx = torch.cat([sink_idx, loc, tail], -1)
+        all_mask = torch.cat([sink_idx >= 0, mine, tail >= 0], -1)
+        idx_new, n_new = _compact(all_mask, all_idx, max_sel, 0)
+        idx_new = idx_new.to(torch.int32).contiguous()
+        sa, ss = lse_sums(scores, idx_new, n_new)
+        O, L, (pa, ps) = yield from draft_output(idx_new, n_new, (sa, ss))
+        self._cached[layer_idx] = (idx_new, n_new)
+        acc = coverage(pa, ps) >= torch.tensor(self.tau, dtype=torch.float32)
+        if not self.lazy:
+            self.stats["heads_accepted"] += int(acc.sum())
+            self.stats["heads_total"] += acc.numel()
+        out = O / L.clamp(min=1e-6).unsqueeze(-1)
+        if bool(acc.all()):
+            return out.to(q.dtype)
+        # exact recovery: rejected heads attend every valid page of the range
+        Wr = scores.shape[-1]
+        every = torch.arange(Wr, device=dev, dtype=torch.int32).view(1, 1, Wr).expand(B, H, Wr)
+        n_rec = torch.where(acc, torch.zeros_like(n_new), nv_r.view(B, 1).to(torch.int32)
+                            .expand(B, H))
+        O2, L2, _ = yield from draft_output(every.contiguous(), n_rec.contiguous())
+        out2 = O2 / L2.clamp(min=1e-6).unsqueeze(-1)
+        acc_q = acc.repeat_interleave(G, dim=1).unsqueeze(-1)
+        return torch.where(acc_q, out, out2).to(q.dtype)

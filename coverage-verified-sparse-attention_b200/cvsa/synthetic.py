@@ -307,3 +307,55 @@ def small(device="cpu", seed: int = 0, B: int = 2, Hq: int = 8, Hkv: int = 2, D:
                   sink_pages=sink_pages, local_pages=local_pages, check_interval=4,
                   meta=dict(seed=seed))
     return wl.to(device)
+
+
+@dataclass
+class RaggedWorkload:
+    """A batch in a paged pool that grows by one token per sequence per step."""
+    name: str
+    cache: object               # cvsa.runtime.kv_cache.PagedKVCache
+    mgr: object                 # cvsa.runtime.kv_cache.SequenceKVManager
+    q: torch.Tensor             # [B, Hq, D] query of every step
+    k_new: torch.Tensor         # [B, Hkv, D] appended token of every step
+    v_new: torch.Tensor
+    budget_pct: float
+    tau: float
+    sink_pages: int
+    local_pages: int
+    check_interval: int
+    meta: Dict = field(default_factory=dict)
+
+
+def config5(device="cuda", seed: int = 0, n_seqs: int = 64, min_len: int = 1024,
+            max_len: int = 65536, grow: int = 256, Hq: int = 32, Hkv: int = 8, D: int = 128,
+            dtype: torch.dtype = torch.bfloat16) -> RaggedWorkload:
+    """Ragged batch: n_seqs sequences with lengths ~ U[min_len, max_len], room
+    to grow by `grow` tokens each, in a pool whose free list is shuffled (pages
+    are handed out in random order, so every table is fragmented). K = 0.1 *
+    N(0, 1), V ~ N(0, 1), no planted pages: attention is diffuse and nearly
+    every head fails tau = 0.9, so scoring steps recover almost every page.
+    The block-table width is the longest possible sequence, so the budget
+    int(W * 0.05) is the same for every sequence (the reference's budget
+    comes from the table width, backend.py:690).
+    """
+    from cvsa.runtime.kv_cache import PagedKVCache, SequenceKVManager
+    bs = 16
+    gc = torch.Generator(device="cpu").manual_seed(seed)
+    lens = torch.randint(min_len, max_len + 1, (n_seqs,), generator=gc)
+    pages = ((lens + grow + bs - 1) // bs).tolist()
+    nb = int(sum(pages)) + n_seqs
+    free = torch.randperm(nb, generator=gc).to(torch.int32)
+    cache = PagedKVCache(nb, bs, Hkv, D, dtype=dtype, device=device, free_list=free)
+    mgr = SequenceKVManager(cache, n_seqs, max_len + grow)
+    g = torch.Generator(device=device).manual_seed(seed + 1)
+    for b in range(n_seqs):
+        n = int(lens[b])
+        k = 0.1 * torch.randn((n, Hkv, D), generator=g, device=device)
+        v = torch.randn((n, Hkv, D), generator=g, device=device)
+        mgr.prefill_kv(b, k.to(dtype), v.to(dtype))
+    q = torch.randn((n_seqs, Hq, D), generator=g, device=device).to(dtype)
+    k_new = (0.1 * torch.randn((n_seqs, Hkv, D), generator=g, device=device)).to(dtype)
+    v_new = torch.randn((n_seqs, Hkv, D), generator=g, device=device).to(dtype)
+    return RaggedWorkload("config5", cache, mgr, q, k_new, v_new, budget_pct=0.05, tau=0.9,
+                          sink_pages=1, local_pages=2, check_interval=4,
+                          meta=dict(seed=seed, lens=lens.tolist(), grow=grow))

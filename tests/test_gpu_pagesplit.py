@@ -1,0 +1,73 @@
+"""Page-split step on the GPU kernels: ranks emulated in one process.
+
+The ranks of a page split (each holding a contiguous range of every
+sequence's pages) run PageSplitBackend with the CUDA kernels; their step
+generators are driven in lockstep, each exchange served by stacking the
+ranks' tensors -- what all_gather returns. Every rank's output must match
+CVSABackend over the whole context within the bf16 bar, and the ranks'
+cached selections, mapped back to global pages, must together be its cached
+selection, across a lazy schedule with rescoring and reuse steps.
+"""
+
+import pytest
+import torch
+
+from cvsa import synthetic
+from cvsa.backend import CVSABackend
+from cvsa.pagesplit import PageSplitBackend, page_range, shard_sequence
+
+pytestmark = pytest.mark.gpu
+
+
+def _lockstep(gens):
+    xs = [next(g) for g in gens]
+    while True:
+        stacked = torch.stack(xs)
+        outs, done = [], 0
+        for g in gens:
+            try:
+                outs.append(g.send(stacked))
+            except StopIteration as e:
+                outs.append(e.value)
+                done += 1
+        if done:
+            assert done == len(gens), "ranks left the exchange at different points"
+            return outs
+        xs = outs
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_page_split_matches_one_gpu(cuda, world):
+    wl = synthetic.small(seed=31, B=2, Hq=32, Hkv=8, D=128, ctx=(9000, 4100), heavy_alpha=4.0,
+                         budget_pct=0.05)
+    d = wl.to(cuda)
+    kw = dict(num_layers=1, budget_pct=0.05, coverage_threshold=0.9, lazy=True,
+              check_interval=2, sink_pages=1, local_pages=2)
+    full = CVSABackend(8, 32, 128, 16, **kw)
+    ranks = []
+    nv = (wl.context_lens.long() + 15) // 16
+    for r in range(world):
+        k, v, bt, cl = shard_sequence(d.k_cache, d.v_cache, d.block_tables, d.context_lens,
+                                      r, world, 16)
+        ranks.append((PageSplitBackend(8, 32, 128, 16, r, world, **kw), k, v, bt, cl,
+                      page_range(nv, r, world)))
+    g = torch.Generator(device="cpu").manual_seed(4)
+    for step in range(6):
+        q = (wl.q.float() + 0.6 * torch.randn(wl.q.shape, generator=g)).to(wl.q.dtype).to(cuda)
+        ref = full(q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        outs = _lockstep([pb.step(q, k, v, bt, cl, 0, d.context_lens, d.block_tables.shape[1])
+                          for pb, k, v, bt, cl, _ in ranks])
+        for out in outs:
+            a, b = out.float(), ref.float()
+            assert ((a - b).abs() <= 2e-2 + 1e-2 * b.abs()).all(), (step, float((a - b).abs().max()))
+        fi, fn = full.cached_selection(0)
+        for b in range(2):
+            for h in range(8):
+                union = []
+                for pb, *_rest, (lo, hi) in ranks:
+                    li, ln = pb.cached_selection(0)
+                    union += [p + int(lo[b]) for p in li[b, h, :int(ln[b, h])].tolist()]
+                assert union == fi[b, h, :int(fn[b, h])].tolist(), (step, b, h)
+        full.step_done(0, 1)
+        for pb, *_ in ranks:
+            pb.step_done(0, 1)
