@@ -429,6 +429,66 @@ def measure_config4(dev, steps, warmup, ws, rank):
             "per_head_accept_rate_rank0": stats.get("per_head_accept_rate")}
 
 
+C3S_LAYERS = 4
+
+
+def measure_config3_split(dev, steps, ws, rank):
+    """Config 3 (one 128K sequence) with its pages split over the ranks
+    (cvsa.pagesplit): every rank scores, selects and attends its contiguous
+    page range; proposals, partials and coverage sums are all-gathered (NCCL)
+    and merged in rank order. Eager (the orchestration is host-side torch
+    around the kernels), lazy M=4 over C3S_LAYERS layers; time per layer-step
+    is the max over ranks."""
+    from cvsa import synthetic
+    from cvsa.pagesplit import PageSplitBackend, dist_allgather, run_step, shard_sequence
+
+    pools = []
+    for l in range(C3S_LAYERS):
+        wl = synthetic.config3(device=dev, seed=3000 + l, gen_device=str(dev))
+        k, v, bt, cl = shard_sequence(wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens,
+                                      rank, ws, 16)
+        pools.append((wl.q, k, v, bt, cl, wl.context_lens, wl.block_tables.shape[1]))
+        del wl
+    torch.cuda.synchronize()
+    pg = None
+    if ws > 1:
+        import torch.distributed as dist
+        pg = dist.group.WORLD
+    pb = PageSplitBackend(8, 32, 128, 16, rank, ws, num_layers=C3S_LAYERS, budget_pct=0.05,
+                          coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
+                          sink_pages=1, local_pages=2, process_group=pg)
+    if ws > 1:
+        ag = dist_allgather(pg)
+    else:
+        def ag(x):
+            return x.unsqueeze(0)
+
+    def one_step():
+        for l, (q, k, v, bt, cl, ctx, W) in enumerate(pools):
+            run_step(pb.step(q, k, v, bt, cl, l, ctx, W), ag)
+            pb.step_done(l, C3S_LAYERS)
+
+    for _ in range(M_INTERVAL):
+        one_step()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    n = max(steps, M_INTERVAL)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        one_step()
+    e1.record()
+    torch.cuda.synchronize()
+    _barrier(ws)
+    ms = _max_over_ranks(e0.elapsed_time(e1), ws)
+    return {"workload": "config3: B=1, Hq=32, Hkv=8, D=128, bf16, ctx=131072 (8192 pages), "
+                        f"pages split contiguously over {ws} GPU(s), lazy M=4, {C3S_LAYERS} layers",
+            "us_per_layer": ms * 1e3 / (n * C3S_LAYERS), "steps": n,
+            "launch": "eager: kernels plus host-side orchestration, NCCL all-gathers",
+            "stats_rank0": dict(pb.stats)}
+
+
 C5_STEPS = 256
 
 
@@ -705,6 +765,9 @@ def run_cvsa(args, ws, rank, local):
     c5 = None
     if not args.no_c5:
         c5 = measure_config5(dev, warm, ws, rank)
+    c3s = None
+    if not args.no_c3:
+        c3s = measure_config3_split(dev, args.steps, ws, rank)
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None
@@ -764,6 +827,8 @@ def run_cvsa(args, ws, rank, local):
             line["config4_70b_head_sharded"] = c4
         if c5 is not None:
             line["config5_ragged_append"] = c5
+        if c3s is not None:
+            line["config3_page_split"] = c3s
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)

@@ -141,11 +141,13 @@ size_t decode_ws(const QView& q, const KvView& kv, int max_sel) {
 
 // Step workspace: [sync region][scores][selection][n][bitmap][gates][partials].
 struct StepLayout {
-  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, comp_cnt, comp_off, attend,
-      total;
+  size_t scores, sel, n, bitmap, acc_new, cov_new, acc_c, cov_c, comp_cnt, comp_off, exp_sel,
+      exp_n, attend, total;
 };
 
-StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense) {
+// exp_stride: row width of the expanded selection (approximate recovery), or 0
+StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recover, bool dense,
+                       int exp_stride = 0) {
   StepLayout L;
   const size_t bh = (size_t)q.B * kv.hkv;
   size_t off = kSyncRegionBytes;
@@ -159,6 +161,8 @@ StepLayout step_layout(const QView& q, const KvView& kv, int max_sel, bool recov
   L.cov_c = off; off += align256(bh * 4);
   L.comp_cnt = off; off += align256(bh * 4);
   L.comp_off = off; off += align256((bh + 1) * 4);
+  L.exp_sel = off; off += align256(bh * (size_t)exp_stride * 4);
+  L.exp_n = off; off += align256(exp_stride > 0 ? bh * 4 : 0);
   L.attend = off; off += attend_workspace_bytes(q, kv, max_sel, recover, dense);
   L.total = off;
   return L;
@@ -390,7 +394,9 @@ size_t cvsa_step_workspace_size(const cvsa_query_desc_t* qd, const cvsa_kv_desc_
   QView q;
   if (check_kv(kvd, &kv) || check_q(qd, kv, false, &q) || !cfg || max_sel <= 0) return 0;
   // size for the largest mode so one workspace serves every mode of a layer
-  StepLayout L = step_layout(q, kv, max_sel, true, false);
+  const int exp_stride = cfg->recovery == CVSA_RECOVERY_APPROX
+                             ? cfg->approx_budget + cfg->sink_pages + cfg->local_pages : 0;
+  StepLayout L = step_layout(q, kv, max_sel, true, false, exp_stride);
   StepLayout Ld = step_layout(q, kv, max_sel, false, true);
   return L.total > Ld.total ? L.total : Ld.total;
 }
@@ -425,8 +431,12 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
     return fail(CVSA_ERR_INVALID, "unknown phase %d", phase);
   if (phase != CVSA_PHASE_ALL && mode != CVSA_MODE_LAZY && mode != CVSA_MODE_SCORE)
     return fail(CVSA_ERR_INVALID, "phases split LAZY and SCORE steps only");
-  if (cfg->recovery != CVSA_RECOVERY_EXACT && cfg->recovery != CVSA_RECOVERY_NONE)
+  if (cfg->recovery != CVSA_RECOVERY_EXACT && cfg->recovery != CVSA_RECOVERY_NONE &&
+      cfg->recovery != CVSA_RECOVERY_APPROX)
     return fail(CVSA_ERR_INVALID, "unknown recovery %d", cfg->recovery);
+  const bool approx = cfg->recovery == CVSA_RECOVERY_APPROX && mode != CVSA_MODE_DENSE;
+  if (approx && cfg->approx_budget <= 0)
+    return fail(CVSA_ERR_INVALID, "approx_budget must be > 0");
   if (cfg->budget < 0 || cfg->sink_pages < 0 || cfg->local_pages < 0)
     return fail(CVSA_ERR_INVALID, "budget/sink/local must be >= 0");
   if (!io->out) return fail(CVSA_ERR_INVALID, "out is NULL");
@@ -449,8 +459,11 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
 
   cudaStream_t s = (cudaStream_t)stream;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-  const bool recover = cfg->recovery == CVSA_RECOVERY_EXACT;
-  StepLayout L = step_layout(q, kv, max_sel, recover || true, dense);
+  const bool recover = cfg->recovery == CVSA_RECOVERY_EXACT || approx;
+  if (approx && !stream_attend_eligible(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "approximate recovery needs a bf16/f16 pool");
+  const int exp_stride = approx ? cfg->approx_budget + cfg->sink_pages + cfg->local_pages : 0;
+  StepLayout L = step_layout(q, kv, max_sel, true, dense, exp_stride);
   void* const* ev = io->timing_events;
   const bool pdl = ev == nullptr;
   auto rec = [&](int i) -> int {
@@ -549,10 +562,32 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   // a decision exchanged between the phases may turn a local reuse into a
   // rescore: keep the complement items either way
   sp.decision_external = phase != CVSA_PHASE_ALL;
+  int32_t* exp_sel = reinterpret_cast<int32_t*>(ws + L.exp_sel);
+  int32_t* exp_n = reinterpret_cast<int32_t*>(ws + L.exp_n);
   if (run_select) {
     if ((st = rec(CVSA_EV_SELECT_BEGIN))) return st;
     st = cuda_status(launch_select_gate(sp, s, pdl), "select launch");
     if (st) return st;
+    if (approx) {
+      // the expanded selection of backend.py:784-797 (same rule, larger budget)
+      SelectParams xp;
+      memset(&xp, 0, sizeof(xp));
+      xp.scores = scores;
+      xp.B = q.B;
+      xp.hkv = kv.hkv;
+      xp.W = q.W;
+      xp.bs = kv.bs;
+      xp.lens = q.lens;
+      xp.budget = cfg->approx_budget;
+      xp.sink = cfg->sink_pages;
+      xp.local = cfg->local_pages;
+      xp.sel_idx = exp_sel;
+      xp.sel_n = exp_n;
+      xp.max_sel = exp_stride;
+      xp.mode = -1;
+      st = cuda_status(launch_select_gate(xp, s, pdl), "expanded select launch");
+      if (st) return st;
+    }
     if ((st = rec(CVSA_EV_SELECT_END))) return st;
   }
   if (!run_attend) return CVSA_OK;
@@ -565,6 +600,10 @@ int cvsa_decode_step(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   ap.src_select = (mode == CVSA_MODE_LAZY) ? 2 : 1;
   ap.decision = sync + 2;
   ap.recover = recover;
+  ap.approx = approx;
+  ap.exp_idx = exp_sel;
+  ap.exp_n = exp_n;
+  ap.exp_stride = exp_stride;
   ap.comp_off = comp_items ? comp_off : nullptr;
   ap.accept = acc_new;
   ap.bitmap = bitmap;

@@ -63,7 +63,10 @@ constexpr uint32_t kSpinLimit = 1u << 22;
 constexpr float kRescaleGap = 8.0f;
 constexpr int kMaxQSlots = 8;  // heads whose query rows a CTA stages in shared memory
 
-enum : int { kKindEmpty = 0, kKindList = 1, kKindRange = 2, kKindRangeSkip = 3 };
+// a head's pages: none; its selection list; every valid page; every valid
+// page outside its selection (bitmap); its expanded selection (approximate
+// recovery)
+enum : int { kKindEmpty = 0, kKindList = 1, kKindRange = 2, kKindRangeSkip = 3, kKindExp = 4 };
 
 struct StreamArgs {
   const void* q;
@@ -87,6 +90,10 @@ struct StreamArgs {
   const float* ext_o;
   const float* ext_m;
   const float* ext_l;
+  int approx;              // rejected heads decode their expanded selection
+  const int32_t* exp_idx;  // [heads][exp_stride]
+  const int32_t* exp_n;
+  int exp_stride;
   int commit;
   int32_t* commit_idx;
   int32_t* commit_n;
@@ -523,9 +530,18 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
       } else {
         const int ns = min(max(src ? n1v : n0v, 0), a.sel_stride);
         const bool rej = a.recover && src == 1 && a.accept[bh] == 0;
-        kind = rej ? kKindRange : kKindList;
-        w = rej ? nv : ns;
-        att += rej ? max(ns, nv) : ns;
+        if (rej && a.approx) {
+          // backend.py:780-817: a rejected head's output is its expanded
+          // selection alone (a superset of its draft)
+          const int ne = min(max(a.exp_n[bh], 0), a.exp_stride);
+          kind = kKindExp;
+          w = ne;
+          att += ne;
+        } else {
+          kind = rej ? kKindRange : kKindList;
+          w = rej ? nv : ns;
+          att += rej ? max(ns, nv) : ns;
+        }
       }
       mx += nv;
       ctxv[h] = ctx;
@@ -685,8 +701,9 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
         const int kind = kindv[h];
         int pg = i;
         bool ok = true;
-        if (kind == kKindList) {
-          pg = sel[(int64_t)bh * a.sel_stride + i];
+        if (kind == kKindList || kind == kKindExp) {
+          pg = kind == kKindList ? sel[(int64_t)bh * a.sel_stride + i]
+                                 : a.exp_idx[(int64_t)bh * a.exp_stride + i];
           if (pg < 0 || pg >= a.W) {
             set_dev_error(a.dev_err, CVSA_DEV_ERR_PAGE_RANGE);
             ok = false;
@@ -1308,6 +1325,10 @@ cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendP
   a.ext_o = p.ext_o;
   a.ext_m = p.ext_m;
   a.ext_l = p.ext_l;
+  a.approx = p.approx ? 1 : 0;
+  a.exp_idx = p.exp_idx;
+  a.exp_n = p.exp_n;
+  a.exp_stride = p.exp_stride;
   a.commit = p.commit_src1 ? 1 : 0;
   a.commit_idx = p.commit_idx;
   a.commit_n = p.commit_n;

@@ -125,6 +125,11 @@ struct AttendParams {
                                   // null: every head's complement chunks are enumerated
   bool external_draft;            // recover_merge: draft partial given, not recomputed
   const float* ext_o; const float* ext_m; const float* ext_l;
+  // approximate recovery: rejected heads decode their expanded selection
+  // (exp_idx / exp_n, rows of exp_stride) instead of every valid page
+  bool approx;
+  const int32_t* exp_idx; const int32_t* exp_n;
+  int exp_stride;
   // copy the source-1 selection into source 0 when source 1 was used
   bool commit_src1;
   int32_t* commit_idx; int32_t* commit_n;

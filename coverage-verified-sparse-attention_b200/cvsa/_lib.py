@@ -25,7 +25,7 @@ LIB_PATH = os.path.join(_HERE, "libcvsa_b200.so")
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 OK, ERR_INVALID, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA, ERR_POOL = 0, -1, -2, -3, -4, -5
 MODE_SCORE, MODE_LAZY, MODE_REUSE, MODE_DENSE = 0, 1, 2, 3
-RECOVERY_EXACT, RECOVERY_NONE = 0, 1
+RECOVERY_EXACT, RECOVERY_NONE, RECOVERY_APPROX = 0, 1, 2
 (CTR_PAGES_ATTENDED, CTR_PAGES_MAX, CTR_HEAD_ACCEPT, CTR_HEAD_TOTAL, CTR_ACCEPT_STEPS,
  CTR_REJECT_STEPS, CTR_SCORING_STEPS, CTR_COVERAGE_CHECKS) = range(8)
 NUM_COUNTERS = 8
@@ -63,6 +63,7 @@ class StepConfig(ctypes.Structure):
         ("sink_pages", ctypes.c_int32), ("local_pages", ctypes.c_int32),
         ("tau", ctypes.c_float), ("recovery", ctypes.c_int32),
         ("has_cache", ctypes.c_int32), ("lazy_stats", ctypes.c_int32),
+        ("approx_budget", ctypes.c_int32),
     ]
 
 

@@ -30,10 +30,13 @@ all-reduced (MIN of one int32) over the group between the selection and the
 attention kernels, so every rank reuses or re-selects together exactly as
 one GPU holding all heads would. Options of the
 reference that select pages differently (adaptive_selection,
-static_budget_table, selector='quest', top_p, light_normalizer), approximate
-recovery, the random-reject counterfactual and the decoupled coverage
-interval are not implemented by this backend yet and raise
-NotImplementedError when requested.
+static_budget_table, selector='quest', top_p, light_normalizer), the
+random-reject counterfactual and the decoupled coverage interval are not
+implemented by this backend yet and raise NotImplementedError when
+requested. Approximate recovery (approx_recovery_pct, backend.py:780-817)
+decodes each rejected head's expanded selection in the same attention
+kernel; the pages-attended statistic counts the pages read (the reference
+also decodes, and counts, the expanded selection of accepted heads).
 """
 
 from __future__ import annotations
@@ -121,8 +124,8 @@ class CVSABackend:
         if sink_pages < 0 or local_pages < 0:
             raise ValueError("sink_pages/local_pages must be >= 0")
         unsupported = []
-        if approx_recovery_pct is not None:
-            unsupported.append("approx_recovery_pct")
+        if approx_recovery_pct is not None and not (0.0 < approx_recovery_pct <= 1.0):
+            raise ValueError(f"approx_recovery_pct must be in (0, 1], got {approx_recovery_pct}")
         if adaptive_selection:
             unsupported.append("adaptive_selection")
         if random_reject_prob is not None:
@@ -344,9 +347,15 @@ class CVSABackend:
         if st.ckey != ckey:
             st.kvd = _lib.kv_desc(k_cache, v_cache)
             st.qd = _lib.query_desc(q, bt, cl)
+            if self.approx_recovery_pct is None:
+                recovery, exp_budget = _lib.RECOVERY_EXACT, 0
+            else:
+                # backend.py:782-783
+                recovery = _lib.RECOVERY_APPROX
+                exp_budget = min(max(budget + 1, int(W * self.approx_recovery_pct)), W)
             st.cfg = _lib.StepConfig(mode, budget, self.sink_pages, self.local_pages,
-                                     float(self.tau), _lib.RECOVERY_EXACT, 0,
-                                     1 if self.lazy else 0)
+                                     float(self.tau), recovery, 0, 1 if self.lazy else 0,
+                                     exp_budget)
             st.io = _lib.StepIO(st.cached_idx.data_ptr(), st.cached_n.data_ptr(), max_sel, 0,
                                 out.data_ptr(), _lib.ptr(st.scores), st.accept.data_ptr(),
                                 st.coverage.data_ptr(), self._counters.data_ptr(),

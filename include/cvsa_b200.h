@@ -200,7 +200,9 @@ enum {
 
 enum {
   CVSA_RECOVERY_EXACT = 0, /* complement + LSE merge (backend.py:818-844) */
-  CVSA_RECOVERY_NONE = 1   /* rejected heads keep the draft */
+  CVSA_RECOVERY_NONE = 1,  /* rejected heads keep the draft */
+  CVSA_RECOVERY_APPROX = 2 /* rejected heads decode an expanded selection of
+                              approx_budget pages (backend.py:780-817) */
 };
 
 /* device counters accumulated by cvsa_decode_step (int64 each) */
@@ -227,6 +229,10 @@ typedef struct cvsa_step_config {
   int32_t lazy_stats;    /* 1: count stats the way lazy mode does
                             (backend.py:420-465), 0: the fixed-interval way
                             (backend.py:775-862) */
+  int32_t approx_budget; /* CVSA_RECOVERY_APPROX: pages of the expanded selection,
+                            min(max(budget + 1, int(max_pages * pct)), max_pages)
+                            (backend.py:782-783); forced pages come on top as in
+                            the draft selection. Needs a bf16/f16 pool. */
 } cvsa_step_config_t;
 
 typedef struct cvsa_step_io {

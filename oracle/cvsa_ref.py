@@ -359,10 +359,21 @@ def selective_lse_merge(o_draft, m_draft, l_draft, o_comp, m_comp, l_comp,
 # a3: one full scoring step; a4: reuse step
 # --------------------------------------------------------------------------
 
+def approx_budget(table_width: int, budget: int, approx_recovery_pct: float) -> int:
+    """Pages of the expanded selection (backend.py:782-783)."""
+    return min(max(budget + 1, int(table_width * approx_recovery_pct)), table_width)
+
+
 def scoring_step(q, k_cache, v_cache, block_tables, context_lens, num_kv_heads,
                  num_q_per_kv, block_size, budget_pct, tau, sink_pages=0, local_pages=0,
-                 page_scores=None, precise=True) -> Dict[str, torch.Tensor]:
-    """cvsa/backend.py:683-864 with exact recovery (complement + LSE merge)."""
+                 page_scores=None, precise=True, approx_recovery_pct=None
+                 ) -> Dict[str, torch.Tensor]:
+    """cvsa/backend.py:683-864: exact recovery (complement + LSE merge), or
+    with approx_recovery_pct the approximate one of backend.py:780-817 (when
+    some head rejects, every head's expanded top-k is attended and rejected
+    heads output it; the expansion follows the same forced-page rule as the
+    draft selection). `n_recovery` is the recovery work the reference records
+    (complement pages of rejected heads, or every head's expanded pages)."""
     W = block_tables.shape[1]
     budget = budget_for(W, budget_pct)
     if page_scores is None:
@@ -374,18 +385,35 @@ def scoring_step(q, k_cache, v_cache, block_tables, context_lens, num_kv_heads,
                                          context_lens, num_kv_heads, num_q_per_kv,
                                          block_size, precise)
     accept, cov = check_coverage(page_scores, idx, nph, tau, precise)
+    exp = None
     if bool(accept.all()):
         out = (o_d / l_d.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
         n_comp = torch.zeros_like(nph)
+        n_rec = n_comp
+    elif approx_recovery_pct is not None:
+        eb = approx_budget(W, budget, approx_recovery_pct)
+        e_idx, e_n = select_pages(page_scores, context_lens, block_size, eb, sink_pages,
+                                  local_pages)
+        o_e, m_e, l_e = sparse_decode_unnorm(q, k_cache, v_cache, block_tables, e_idx, e_n,
+                                             context_lens, num_kv_heads, num_q_per_kv,
+                                             block_size, precise)
+        acc_q = accept.repeat_interleave(num_q_per_kv, dim=1).unsqueeze(-1)
+        out = torch.where(acc_q, o_d / l_d.clamp(min=1e-6).unsqueeze(-1),
+                          o_e / l_e.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
+        n_comp = torch.zeros_like(nph)
+        n_rec = e_n
+        exp = (e_idx, e_n)
     else:
         comp, n_comp = compute_complement_pages(idx, nph, context_lens, block_size, accept)
         o_c, m_c, l_c = sparse_decode_unnorm(q, k_cache, v_cache, block_tables, comp, n_comp,
                                              context_lens, num_kv_heads, num_q_per_kv,
                                              block_size, precise)
         out = selective_lse_merge(o_d, m_d, l_d, o_c, m_c, l_c, accept, num_q_per_kv, q.dtype)
+        n_rec = n_comp
     return dict(output=out, page_scores=page_scores, page_indices=idx, n_per_head=nph,
                 accept=accept, coverage=cov, o_draft=o_d, m_draft=m_d, l_draft=l_d,
-                n_complement=n_comp, budget=torch.tensor(budget))
+                n_complement=n_comp, n_recovery=n_rec, expanded=exp,
+                budget=torch.tensor(budget))
 
 
 class OracleBackend:
@@ -401,7 +429,7 @@ class OracleBackend:
     def __init__(self, num_kv_heads, num_q_heads, head_dim, block_size, num_layers=32,
                  budget_pct=0.10, reuse_interval=16, coverage_threshold=0.90,
                  dense_layers=None, lazy=False, check_interval=None,
-                 sink_pages=0, local_pages=0, precise=True):
+                 sink_pages=0, local_pages=0, precise=True, approx_recovery_pct=None):
         self.num_kv_heads = num_kv_heads
         self.num_q_heads = num_q_heads
         self.G = num_q_heads // num_kv_heads
@@ -417,6 +445,7 @@ class OracleBackend:
         self.sink_pages = sink_pages
         self.local_pages = local_pages
         self.precise = precise
+        self.approx_recovery_pct = approx_recovery_pct
         self.reset()
 
     def reset(self):
@@ -451,9 +480,9 @@ class OracleBackend:
     def _scoring(self, q, k, v, bt, cl, layer_idx, page_scores=None):
         r = scoring_step(q, k, v, bt, cl, self.num_kv_heads, self.G, self.block_size,
                          self.budget_pct, self.tau, self.sink_pages, self.local_pages,
-                         page_scores, self.precise)
+                         page_scores, self.precise, self.approx_recovery_pct)
         self._cached[layer_idx] = (r["page_indices"], r["n_per_head"])
-        self._record(cl, r["n_per_head"].sum() + r["n_complement"].sum())
+        self._record(cl, r["n_per_head"].sum() + r["n_recovery"].sum())
         self.total_scoring_steps += 1
         if not self.lazy:
             self.per_head_accept_sum += int(r["accept"].sum())

@@ -95,7 +95,10 @@ def test_backend_argument_checks_match_reference():
     with pytest.raises(ValueError):
         CVSABackend(8, 32, 128, 16, top_p=1.5)
     with pytest.raises(NotImplementedError):
-        CVSABackend(8, 32, 128, 16, approx_recovery_pct=0.2)
+        CVSABackend(8, 32, 128, 16, adaptive_selection=True)
+    with pytest.raises(ValueError):
+        CVSABackend(8, 32, 128, 16, approx_recovery_pct=1.5)
+    CVSABackend(8, 32, 128, 16, approx_recovery_pct=0.2)     # supported
 
 
 def test_budget_uses_table_width():

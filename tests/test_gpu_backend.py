@@ -243,3 +243,55 @@ def test_step_is_graph_capturable_and_deterministic(cuda):
     torch.cuda.synchronize()
     # same q, same cache: the replayed lazy step reproduces the first step exactly
     assert torch.equal(out, first)
+
+
+def test_approx_recovery_lazy_matches_reference(cuda):
+    """approx_recovery_pct=0.2 over a lazy schedule against the reference's own
+    CVSABackend outputs (tests/golden/make_golden_ar.py; every head rejects at
+    tau=0.95, so each check step decodes the expanded selections)."""
+    import os
+    from conftest import GOLDEN
+    g = dict(np.load(os.path.join(os.path.dirname(GOLDEN), "reference_outputs_ar.npz")))
+    wl = synthetic.small(seed=3, B=2, Hq=8, Hkv=2, D=128, ctx=(1000, 2048))
+    d = wl.to(cuda)
+    be = CVSABackend(num_kv_heads=2, num_q_heads=8, head_dim=128, block_size=16, num_layers=1,
+                     budget_pct=wl.budget_pct, coverage_threshold=0.95, lazy=True,
+                     check_interval=2, approx_recovery_pct=0.2)
+    for step in range(4):
+        q = torch.from_numpy(g[f"small_ar20_q{step}"]).to(torch.bfloat16).to(cuda)
+        out = be(q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        be.step_done(0, 1)
+        _close(out, g[f"small_ar20_out{step}"], torch.bfloat16)
+    st = be.get_stats()
+    for key in ("total_scoring_steps", "total_coverage_checks", "per_head_accept_rate"):
+        assert abs(st[key] - float(g["small_ar20_stat_" + key])) < 1e-9, key
+
+
+def test_approx_recovery_vs_oracle(cuda):
+    """Approximate recovery with forced pages, Llama-8B head geometry, lazy
+    schedule with drifting queries: outputs, cached selections and decisions
+    against the oracle backend."""
+    wl = synthetic.small(seed=12, B=2, Hq=32, Hkv=8, D=128, ctx=(6000, 2500), heavy_alpha=3.0)
+    d = wl.to(cuda)
+    kw = dict(num_layers=1, budget_pct=0.05, coverage_threshold=0.9, lazy=True, check_interval=2,
+              sink_pages=1, local_pages=2, approx_recovery_pct=0.2)
+    be = CVSABackend(8, 32, 128, 16, **kw)
+    ob = R.OracleBackend(8, 32, 128, 16, **kw)
+    g = torch.Generator().manual_seed(6)
+    rejected = 0
+    for step in range(6):
+        q = (wl.q.float() + 0.8 * torch.randn(wl.q.shape, generator=g)).to(wl.q.dtype)
+        out = be(q.to(cuda), d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        ref = ob(q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+        _close(out, ref, wl.q.dtype)
+        if "accept" in ob.last and ob.last.get("expanded") is not None:
+            rejected += int((~ob.last["accept"]).sum())
+        gi, gn = be.cached_selection(0)
+        oi, on = ob._cached[0]
+        assert sel_sets(gi.cpu(), gn.cpu()) == sel_sets(oi, on), step
+        be.step_done(0, 1)
+        ob.step_done(0, 1)
+    assert rejected > 0, "no head took the approximate branch"
+    gs, os_ = be.get_stats(), ob.get_stats()
+    for key in ("total_scoring_steps", "total_coverage_checks", "per_head_accept_rate"):
+        assert abs(gs[key] - os_[key]) < 1e-9, (key, gs[key], os_[key])

@@ -6,11 +6,13 @@ interpreter on the same seeded inputs. These tests pin the oracle (the checker
 of every GPU parity test) to the reference.
 """
 
+import os
+
 import numpy as np
 import pytest
 import torch
 
-from conftest import finite_close, input_checksum, sel_sets
+from conftest import GOLDEN, finite_close, input_checksum, sel_sets
 from cvsa import synthetic
 from oracle import cvsa_ref as R
 
@@ -104,3 +106,47 @@ def test_oracle_lazy_schedule_matches_reference(golden):
     for key in ("total_scoring_steps", "total_coverage_checks", "all_accepted_pct",
                 "some_rejected_pct", "per_head_accept_rate", "effective_budget_pct"):
         assert abs(st[key] - float(golden["small_lazy_stat_" + key])) < 1e-9, key
+
+
+@pytest.fixture(scope="module")
+def golden_ar():
+    return dict(np.load(os.path.join(os.path.dirname(GOLDEN), "reference_outputs_ar.npz")))
+
+
+def test_oracle_approx_recovery_matches_reference(golden_ar):
+    """approx_recovery_pct=0.2 (backend.py:780-817) against the reference's
+    own CVSABackend (tests/golden/make_golden_ar.py): output, expanded
+    selection, accept mask and the recorded work."""
+    wl = synthetic.config1()
+    be = R.OracleBackend(2, 8, 64, 16, num_layers=1, budget_pct=wl.budget_pct,
+                         coverage_threshold=wl.tau, approx_recovery_pct=0.2)
+    out = be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+    e_idx, e_n = be.last["expanded"]
+    assert np.array_equal(e_n.numpy(), golden_ar["config1_ar20_exp_n"])
+    assert sel_sets(e_idx, e_n) == [[list(r[:int(k)]) for r, k in zip(rows, ns)]
+                                    for rows, ns in zip(golden_ar["config1_ar20_exp_sel"],
+                                                        golden_ar["config1_ar20_exp_n"])]
+    assert np.array_equal(be.last["accept"].numpy().astype(np.uint8),
+                          golden_ar["config1_ar20_accept"])
+    assert not bool(be.last["accept"].all())          # the approximate branch ran
+    assert (out - torch.from_numpy(golden_ar["config1_ar20_output"])).abs().max() < 1e-4
+    st = be.get_stats()
+    assert abs(st["effective_budget_pct"]
+               - float(golden_ar["config1_ar20_stat_effective_budget_pct"])) < 1e-9
+
+
+def test_oracle_approx_recovery_lazy_matches_reference(golden_ar):
+    wl = synthetic.small(seed=3, B=2, Hq=8, Hkv=2, D=128, ctx=(1000, 2048))
+    be = R.OracleBackend(2, 8, 128, 16, num_layers=1, budget_pct=wl.budget_pct,
+                         coverage_threshold=0.95, lazy=True, check_interval=2,
+                         approx_recovery_pct=0.2)
+    for step in range(4):
+        q = torch.from_numpy(golden_ar[f"small_ar20_q{step}"]).to(torch.bfloat16)
+        out = be(q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+        be.step_done(0, 1)
+        ref = torch.from_numpy(golden_ar[f"small_ar20_out{step}"])
+        assert (out.float() - ref).abs().max() < 2e-2, step
+    st = be.get_stats()
+    for key in ("total_scoring_steps", "total_coverage_checks", "per_head_accept_rate",
+                "effective_budget_pct"):
+        assert abs(st[key] - float(golden_ar["small_ar20_stat_" + key])) < 1e-9, key
