@@ -62,19 +62,63 @@ def _peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU, sampled
+    through NVML every 2 ms from a thread while the timed region runs, plus
+    one sample when it starts and one when it ends (the config-2 region is
+    about 15 ms, shorter than nvidia-smi's sampling period). The GPU is found
+    by UUID, so CUDA_VISIBLE_DEVICES cannot point it at another device;
+    without NVML, nvidia-smi is polled instead."""
 
+    # NVML clock-event reason bits (nvml.h nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
+        self.nv = None
+        self.handle = None
+        self.samples = []        # (sm_mhz, reason bits)
+        self.smax = None
         self.proc = None
         self.lines = []
         self.t = None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:
+                uuid = str(torch.cuda.get_device_properties(index).uuid)
+                uuid = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+                self.handle = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            except Exception:
+                self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+        except Exception:
+            self.nv = None
+
+    def _sample(self):
+        nv, h = self.nv, self.handle
+        try:
+            fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            self.samples.append((float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)), int(fn(h))))
+        except Exception:
+            pass
+
+    def _poll(self):
+        while not self._stop.wait(0.002):
+            self._sample()
 
     def start(self):
+        if self.nv is not None:
+            self._sample()
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
@@ -90,8 +134,19 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nv is not None:
+            self._stop.set()
+            self.t.join(timeout=5)
+            self._sample()
+            sm = [c for c, _ in self.samples]
+            bits = 0
+            for _, r in self.samples:
+                bits |= r
+            reasons = sorted(nm for bit, nm in self.REASONS.items() if bits & bit)
+            return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax,
+                    "reasons": reasons, "samples": len(sm), "source": "NVML, 2 ms"}
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -112,7 +167,7 @@ class ClockSampler:
                 if val.lower() == "active":
                     reasons.add(nm)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi"}
 
 
 def _dist():
@@ -738,12 +793,33 @@ def run_cvsa(args, ws, rank, local):
     out_host = [torch.empty_like(h).pin_memory() for h in q_host]
     q_dev = [torch.empty_like(wl.q) for wl in wls]
 
+    # Every step uploads each layer's q from pinned memory and reads each
+    # layer's output back, all inside the timed region. The uploads run on a
+    # copy stream (layer l's step waits only for its own q) and each output
+    # is read back on a second copy stream as soon as its layer is done, so
+    # the copies overlap the other layers' kernels; the step ends when the
+    # last read-back has landed.
+    comp = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    q_ready = [torch.cuda.Event() for _ in wls]
+    o_ready = [torch.cuda.Event() for _ in wls]
+
     def e2e_step(_s=0):
+        up.wait_stream(comp)              # the previous step's layers are done with q_dev
+        with torch.cuda.stream(up):
+            for l in range(layers):
+                q_dev[l].copy_(q_host[l], non_blocking=True)
+                q_ready[l].record(up)
         for l, wl in enumerate(wls):
-            q_dev[l].copy_(q_host[l], non_blocking=True)
+            comp.wait_event(q_ready[l])
             o = be3(q_dev[l], wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, l)
-            out_host[l].copy_(o, non_blocking=True)
+            o_ready[l].record(comp)
+            down.wait_event(o_ready[l])
+            with torch.cuda.stream(down):
+                out_host[l].copy_(o, non_blocking=True)
+                o.record_stream(down)
             be3.step_done(l, layers)
+        comp.wait_stream(down)
 
     for _ in range(warm):
         e2e_step()
@@ -817,7 +893,9 @@ def run_cvsa(args, ws, rank, local):
                            if k in stats},
             "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": h2d, "ms_per_step": ms_e / args.steps,
-                    "path": "CVSABackend.__call__ per layer (eager), pinned H2D q, D2H output"},
+                    "path": "CVSABackend.__call__ per layer (eager); every layer's q uploaded "
+                            "from pinned memory and its output read back each step, on copy "
+                            "streams overlapping the other layers' kernels"},
             "gpu_launches": launches,
             "clocks": clk,
         }

@@ -30,10 +30,12 @@ all-reduced (MIN of one int32) over the group between the selection and the
 attention kernels, so every rank reuses or re-selects together exactly as
 one GPU holding all heads would. Options of the
 reference that select pages differently (adaptive_selection,
-static_budget_table, selector='quest', top_p, light_normalizer), the
-random-reject counterfactual and the decoupled coverage interval are not
-implemented by this backend yet and raise NotImplementedError when
-requested. Approximate recovery (approx_recovery_pct, backend.py:780-817)
+static_budget_table, selector='quest', top_p, light_normalizer) and the
+random-reject counterfactual are not implemented by this backend yet and
+raise NotImplementedError when requested. A coverage_interval below
+check_interval runs the reference's coverage-only steps (backend.py:467-520):
+the cached selection is gated on the page scores kept from the last scoring
+step, and the host reads the decision, as the reference does. Approximate recovery (approx_recovery_pct, backend.py:780-817)
 decodes each rejected head's expanded selection in the same attention
 kernel; the pages-attended statistic counts the pages read (the reference
 also decodes, and counts, the expanded selection of accepted heads).
@@ -52,7 +54,8 @@ from cvsa.kernels.select import budget_for
 
 class _LayerState:
     __slots__ = ("key", "cached_idx", "cached_n", "has_cache", "accept", "accept_bool",
-                 "coverage", "flags", "scores", "ckey", "kvd", "qd", "cfg", "io", "ws_bytes")
+                 "coverage", "flags", "scores", "ckey", "kvd", "qd", "cfg", "io", "ws_bytes",
+                 "scored", "has_scored")
 
     def __init__(self, key, B, Hkv, max_sel, W, device, keep_scores):
         self.key = key
@@ -66,6 +69,12 @@ class _LayerState:
         self.flags = torch.zeros((1,), dtype=torch.int32, device=device)
         self.scores = (torch.empty((B, Hkv, W), dtype=torch.float32, device=device)
                        if keep_scores else None)
+        # page scores of the last scoring step (coverage-only steps gate on them)
+        self.scored = None
+        self.has_scored = False
+
+
+_MODE_COVERAGE_ONLY = -100   # host-side marker: gate on cached scores, then reuse or rescore
 
 
 class StepHandle:
@@ -136,8 +145,6 @@ class CVSABackend:
             unsupported.append("selector='quest'")
         if top_p is not None:
             unsupported.append("top_p")
-        if lazy and coverage_interval is not None and coverage_interval != (check_interval or 1):
-            unsupported.append("coverage_interval != check_interval")
         if unsupported:
             raise NotImplementedError("not implemented by the B200 backend: " +
                                       ", ".join(unsupported))
@@ -284,9 +291,16 @@ class CVSABackend:
         key = (B, W, max_sel, device)
         st = self._layers.get(layer_idx)
         if st is None or st.key != key:
-            st = _LayerState(key, B, self.num_kv_heads, max_sel, W, device, self.keep_page_scores)
+            cv = self._coverage_only_enabled()
+            st = _LayerState(key, B, self.num_kv_heads, max_sel, W, device,
+                             self.keep_page_scores or cv)
+            if cv:
+                st.scored = torch.empty_like(st.scores)
             self._layers[layer_idx] = st
         return st
+
+    def _coverage_only_enabled(self) -> bool:
+        return self.lazy and self.coverage_interval != self.check_interval
 
     def _mode_for(self, layer_idx: int, st: _LayerState) -> int:
         if layer_idx in self._dense_layers:
@@ -294,6 +308,9 @@ class CVSABackend:
         if self.lazy:
             if self._step % self.check_interval == 0 or not st.has_cache:
                 return _lib.MODE_LAZY
+            if (self._step % self.coverage_interval == 0 and st.has_scored
+                    and self._coverage_only_enabled()):
+                return _MODE_COVERAGE_ONLY
             return _lib.MODE_REUSE
         if self._step % self.reuse_interval == 0 or not st.has_cache:
             return _lib.MODE_SCORE
@@ -329,6 +346,8 @@ class CVSABackend:
         max_sel = budget + self.sink_pages + self.local_pages
         st = self._layer_state(layer_idx, B, W, max_sel, dev)
         mode = self._mode_for(layer_idx, st)
+        if mode == _MODE_COVERAGE_ONLY:
+            mode = self._coverage_only(st, layer_idx)
         if mode == _lib.MODE_DENSE:
             self._dense_layer_steps += 1
 
@@ -402,7 +421,32 @@ class CVSABackend:
         if mode in (_lib.MODE_SCORE, _lib.MODE_LAZY):
             st.has_cache = True
             self._last_accept_mask[layer_idx] = st.accept_bool
+            if st.scored is not None:
+                # keep this step's scores if it rescored (step_flags bit1), as
+                # the reference caches page_scores in _scoring_step only
+                # (backend.py:713); decided on the device
+                rescored = (st.flags & 2).bool()
+                torch.where(rescored, st.scores, st.scored, out=st.scored)
+                st.has_scored = True
         return handle
+
+    def _coverage_only(self, st: _LayerState, layer_idx: int) -> int:
+        """backend.py:467-520: gate the cached selection on the page scores of
+        the last scoring step, without scoring. Returns the step to run:
+        REUSE if every head accepts, else SCORE (fresh scores). The decision is
+        read on the host, as the reference does (`accept_mask.all()`)."""
+        from cvsa.kernels.coverage import check_coverage
+        acc, _cov = check_coverage(st.scored, st.cached_idx, st.cached_n, self.tau)
+        c = self._counters
+        c[_lib.CTR_HEAD_ACCEPT] += acc.sum()
+        c[_lib.CTR_HEAD_TOTAL] += acc.numel()
+        c[_lib.CTR_COVERAGE_CHECKS] += 1
+        if bool(acc.all()):
+            c[_lib.CTR_ACCEPT_STEPS] += 1
+            self._last_accept_mask[layer_idx] = acc
+            return _lib.MODE_REUSE
+        c[_lib.CTR_REJECT_STEPS] += 1
+        return _lib.MODE_SCORE
 
     def finish_step(self, h: "StepHandle") -> torch.Tensor:
         """Run the attention half of a phased step (after its decision word

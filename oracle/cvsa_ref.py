@@ -429,7 +429,8 @@ class OracleBackend:
     def __init__(self, num_kv_heads, num_q_heads, head_dim, block_size, num_layers=32,
                  budget_pct=0.10, reuse_interval=16, coverage_threshold=0.90,
                  dense_layers=None, lazy=False, check_interval=None,
-                 sink_pages=0, local_pages=0, precise=True, approx_recovery_pct=None):
+                 sink_pages=0, local_pages=0, precise=True, approx_recovery_pct=None,
+                 coverage_interval=None):
         self.num_kv_heads = num_kv_heads
         self.num_q_heads = num_q_heads
         self.G = num_q_heads // num_kv_heads
@@ -446,11 +447,13 @@ class OracleBackend:
         self.local_pages = local_pages
         self.precise = precise
         self.approx_recovery_pct = approx_recovery_pct
+        self.coverage_interval = coverage_interval or self.check_interval
         self.reset()
 
     def reset(self):
         self._step = 0
         self._cached: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+        self._cached_scores: Dict[int, torch.Tensor] = {}   # backend.py:713
         self.attn_work = 0
         self.attn_work_max = 0
         self.accept_counts = 0
@@ -482,6 +485,7 @@ class OracleBackend:
                          self.budget_pct, self.tau, self.sink_pages, self.local_pages,
                          page_scores, self.precise, self.approx_recovery_pct)
         self._cached[layer_idx] = (r["page_indices"], r["n_per_head"])
+        self._cached_scores[layer_idx] = r["page_scores"]
         self._record(cl, r["n_per_head"].sum() + r["n_recovery"].sum())
         self.total_scoring_steps += 1
         if not self.lazy:
@@ -502,12 +506,33 @@ class OracleBackend:
             return dense_decode(q, k, v, bt, cl, self.num_kv_heads, self.G,
                                 self.block_size, self.precise)
         if self.lazy:
+            # backend.py:335-358: scoring every check_interval steps, the
+            # coverage-only gate every coverage_interval steps in between
             if self._step % self.check_interval == 0 or layer_idx not in self._cached:
                 return self._lazy(q, k, v, bt, cl, layer_idx)
+            if self._step % self.coverage_interval == 0 and layer_idx in self._cached_scores:
+                return self._coverage_only(q, k, v, bt, cl, layer_idx)
             return self._reuse(q, k, v, bt, cl, layer_idx)
         if self._step % self.reuse_interval == 0 or layer_idx not in self._cached:
             return self._scoring(q, k, v, bt, cl, layer_idx)
         return self._reuse(q, k, v, bt, cl, layer_idx)
+
+    def _coverage_only(self, q, k, v, bt, cl, layer_idx):
+        """backend.py:467-520: gate the cached selection on the page scores of
+        the last scoring step (no fresh scores); reuse it if every head
+        accepts, else a scoring step on fresh scores."""
+        idx, nph = self._cached[layer_idx]
+        accept, cov = check_coverage(self._cached_scores[layer_idx], idx, nph, self.tau,
+                                     self.precise)
+        self.per_head_accept_sum += int(accept.sum())
+        self.per_head_total += accept.numel()
+        self.total_coverage_checks += 1
+        self.last = dict(cached_accept=accept, cached_coverage=cov)
+        if bool(accept.all()):
+            self.accept_counts += 1
+            return self._reuse(q, k, v, bt, cl, layer_idx)
+        self.reject_counts += 1
+        return self._scoring(q, k, v, bt, cl, layer_idx)
 
     def _lazy(self, q, k, v, bt, cl, layer_idx):
         scores = score_pages(q, k, bt, cl, self.num_kv_heads, self.G, self.block_size,

@@ -295,3 +295,53 @@ def test_approx_recovery_vs_oracle(cuda):
     gs, os_ = be.get_stats(), ob.get_stats()
     for key in ("total_scoring_steps", "total_coverage_checks", "per_head_accept_rate"):
         assert abs(gs[key] - os_[key]) < 1e-9, (key, gs[key], os_[key])
+
+
+def test_coverage_only_steps_match_reference(cuda):
+    """coverage_interval=2 < check_interval=4: coverage-only steps gate the
+    cached selection on the last scoring step's page scores (backend.py:
+    467-520); outputs and statistics against the reference's own CVSABackend
+    (tests/golden/make_golden_cv.py)."""
+    import os
+    from conftest import GOLDEN
+    g = dict(np.load(os.path.join(os.path.dirname(GOLDEN), "reference_outputs_cv.npz")))
+    wl = synthetic.small(seed=3, B=2, Hq=8, Hkv=2, D=128, ctx=(1000, 2048))
+    d = wl.to(cuda)
+    be = CVSABackend(num_kv_heads=2, num_q_heads=8, head_dim=128, block_size=16, num_layers=1,
+                     budget_pct=wl.budget_pct, coverage_threshold=0.16, lazy=True,
+                     check_interval=4, coverage_interval=2)
+    for step in range(9):
+        q = torch.from_numpy(g[f"small_cv_q{step}"]).to(torch.bfloat16).to(cuda)
+        out = be(q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        be.step_done(0, 1)
+        _close(out, g[f"small_cv_out{step}"], torch.bfloat16)
+    st = be.get_stats()
+    for key in ("total_scoring_steps", "total_coverage_checks", "all_accepted_pct",
+                "some_rejected_pct", "per_head_accept_rate", "effective_budget_pct"):
+        assert abs(st[key] - float(g["small_cv_stat_" + key])) < 1e-9, key
+
+
+def test_coverage_only_steps_vs_oracle(cuda):
+    """Coverage-only steps with forced pages and Llama-8B head geometry,
+    against the oracle backend: outputs, cached selections, statistics."""
+    wl = synthetic.small(seed=14, B=2, Hq=32, Hkv=8, D=128, ctx=(5000, 3100), heavy_alpha=5.0)
+    d = wl.to(cuda)
+    kw = dict(num_layers=1, budget_pct=0.05, coverage_threshold=0.5, lazy=True, check_interval=4,
+              coverage_interval=2, sink_pages=1, local_pages=2)
+    be = CVSABackend(8, 32, 128, 16, **kw)
+    ob = R.OracleBackend(8, 32, 128, 16, **kw)
+    g = torch.Generator().manual_seed(8)
+    for step in range(10):
+        q = (wl.q.float() + 0.5 * torch.randn(wl.q.shape, generator=g)).to(wl.q.dtype)
+        out = be(q.to(cuda), d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        ref = ob(q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+        _close(out, ref, wl.q.dtype)
+        gi, gn = be.cached_selection(0)
+        oi, on = ob._cached[0]
+        assert sel_sets(gi.cpu(), gn.cpu()) == sel_sets(oi, on), step
+        be.step_done(0, 1)
+        ob.step_done(0, 1)
+    gs, os_ = be.get_stats(), ob.get_stats()
+    for key in ("total_scoring_steps", "total_coverage_checks", "all_accepted_pct",
+                "some_rejected_pct", "per_head_accept_rate", "effective_budget_pct"):
+        assert abs(gs[key] - os_[key]) < 1e-9, (key, gs[key], os_[key])

@@ -150,3 +150,22 @@ def test_oracle_approx_recovery_lazy_matches_reference(golden_ar):
     for key in ("total_scoring_steps", "total_coverage_checks", "per_head_accept_rate",
                 "effective_budget_pct"):
         assert abs(st[key] - float(golden_ar["small_ar20_stat_" + key])) < 1e-9, key
+
+
+def test_oracle_coverage_only_steps_match_reference():
+    """coverage_interval=2 < check_interval=4 (backend.py:467-520) against the
+    reference's own CVSABackend (tests/golden/make_golden_cv.py)."""
+    g = dict(np.load(os.path.join(os.path.dirname(GOLDEN), "reference_outputs_cv.npz")))
+    wl = synthetic.small(seed=3, B=2, Hq=8, Hkv=2, D=128, ctx=(1000, 2048))
+    be = R.OracleBackend(2, 8, 128, 16, num_layers=1, budget_pct=wl.budget_pct,
+                         coverage_threshold=0.16, lazy=True, check_interval=4,
+                         coverage_interval=2)
+    for step in range(9):
+        q = torch.from_numpy(g[f"small_cv_q{step}"]).to(torch.bfloat16)
+        out = be(q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+        be.step_done(0, 1)
+        assert (out.float() - torch.from_numpy(g[f"small_cv_out{step}"])).abs().max() < 2e-2, step
+    st = be.get_stats()
+    for key in ("total_scoring_steps", "total_coverage_checks", "all_accepted_pct",
+                "some_rejected_pct", "per_head_accept_rate", "effective_budget_pct"):
+        assert abs(st[key] - float(g["small_cv_stat_" + key])) < 1e-9, key
