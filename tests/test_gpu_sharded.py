@@ -1,11 +1,12 @@
-"""Head-sharded steps on one GPU: two shards, each a backend holding half of
-the KV heads (and their query heads), run the phased lazy step through
-begin_step / finish_step with their decision words combined by MIN between
-the halves -- what two ranks do with an all-reduce -- and must reproduce one
-backend holding every head: identical cached selections, outputs within the
-bf16 bar, the same reuse / rescore choices. The check step is built so one
-shard's heads all accept their cached selection while the other's reject,
-so the combined decision differs from one shard's own.
+"""Head-sharded steps on one GPU: 2 or 8 shards, each a backend holding an
+equal block of the KV heads (and their query heads; 8 shards leave one KV
+head per shard, as on 8 GPUs), run the phased lazy step through begin_step /
+finish_step with their decision words combined by MIN between the halves --
+what the ranks do with an all-reduce -- and must reproduce one backend
+holding every head: identical cached selections, outputs within the bf16
+bar, the same reuse / rescore choices. The check step is built so the first
+half of the heads accept their cached selection while the rest reject, so
+the combined decision differs from some shards' own.
 """
 
 import pytest
@@ -24,7 +25,8 @@ def _close(a, b):
     assert ((a - b).abs() <= 2e-2 + 1e-2 * b.abs()).all(), float((a - b).abs().max())
 
 
-def test_two_shards_match_one_backend(cuda):
+@pytest.mark.parametrize("world", [2, 8])
+def test_shards_match_one_backend(cuda, world):
     Hkv, Hq, D = 8, 32, 128
     wl = synthetic.small(seed=11, B=2, Hq=Hq, Hkv=Hkv, D=D, ctx=(4096, 2500), heavy_alpha=5.0)
     d = wl.to(cuda)
@@ -47,9 +49,9 @@ def test_two_shards_match_one_backend(cuda):
               lazy=True, check_interval=2, sink_pages=1, local_pages=2)
     full = CVSABackend(Hkv, Hq, **kw)
     shards = []
-    for r in range(2):
-        kv_s, q_s = shard_heads(Hkv, Hq, r, 2)
-        be = CVSABackend(Hkv // 2, Hq // 2, **kw)
+    for r in range(world):
+        kv_s, q_s = shard_heads(Hkv, Hq, r, world)
+        be = CVSABackend(Hkv // world, Hq // world, **kw)
         shards.append((be, kv_s, q_s, d.k_cache[:, :, kv_s].contiguous(),
                        d.v_cache[:, :, kv_s].contiguous()))
 
@@ -64,8 +66,10 @@ def test_two_shards_match_one_backend(cuda):
                    for be, kv_s, q_s, kc, vc in shards]
         if handles[0].decision is not None:
             local = [int(h.decision.item()) for h in handles]
-            saw_split_decision |= local[0] != local[1]
-            combined = torch.minimum(handles[0].decision, handles[1].decision)
+            saw_split_decision |= len(set(local)) > 1
+            combined = handles[0].decision.clone()
+            for h in handles[1:]:
+                combined = torch.minimum(combined, h.decision)
             for h in handles:
                 h.decision.copy_(combined)
             for (be, *_), h in zip(shards, handles):
