@@ -491,9 +491,10 @@ def measure_config3_split(dev, steps, ws, rank):
     """Config 3 (one 128K sequence) with its pages split over the ranks
     (cvsa.pagesplit): every rank scores, selects and attends its contiguous
     page range; proposals, partials and coverage sums are all-gathered (NCCL)
-    and merged in rank order. Eager (the orchestration is host-side torch
-    around the kernels), lazy M=4 over C3S_LAYERS layers; time per layer-step
-    is the max over ranks."""
+    and merged in rank order. Lazy M=4 over C3S_LAYERS layers; the lazy-check
+    step and the reuse step (all layers each) are captured as CUDA graphs with
+    the all-gathers inside and timed separately; times are the max over
+    ranks."""
     from cvsa import synthetic
     from cvsa.pagesplit import PageSplitBackend, dist_allgather, run_step, shard_sequence
 
@@ -523,25 +524,67 @@ def measure_config3_split(dev, steps, ws, rank):
             run_step(pb.step(q, k, v, bt, cl, l, ctx, W), ag)
             pb.step_done(l, C3S_LAYERS)
 
-    for _ in range(M_INTERVAL):
-        one_step()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    graphs = {}
+    with torch.cuda.stream(side):
+        for _ in range(M_INTERVAL + 1):
+            one_step()
+        side.synchronize()
+        # the eager warm-up steps' counts (a replayed graph advances only the
+        # device-side counters)
+        stats = pb.stats
+        ok = 1
+        try:
+            for kind, step_idx in (("check", 0), ("reuse", 1)):
+                g = torch.cuda.CUDAGraph()
+                pb._step = step_idx
+                with torch.cuda.graph(g, stream=side):
+                    for l, (q, k, v, bt, cl, ctx, W) in enumerate(pools):
+                        run_step(pb.step(q, k, v, bt, cl, l, ctx, W), ag)
+                graphs[kind] = g
+        except Exception:  # noqa: BLE001 - capture unsupported here: time eager steps
+            ok = 0
+    torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize()
-    _barrier(ws)
-    n = max(steps, M_INTERVAL)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(n):
-        one_step()
-    e1.record()
-    torch.cuda.synchronize()
-    _barrier(ws)
-    ms = _max_over_ranks(e0.elapsed_time(e1), ws)
+    if ws > 1:
+        t = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = int(t.item())
+    if not ok:
+        graphs = {}
+
+    def run(kind, n):
+        for _ in range(n):
+            if graphs:
+                graphs[kind].replay()
+            else:
+                pb._step = 0 if kind == "check" else 1
+                one_step()
+
+    res = {}
+    n = max(steps // 2, 2)
+    for kind in ("check", "reuse"):
+        run(kind, 1)
+        torch.cuda.synchronize()
+        _barrier(ws)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        run(kind, n)
+        e1.record()
+        torch.cuda.synchronize()
+        _barrier(ws)
+        res[kind] = _max_over_ranks(e0.elapsed_time(e1), ws) * 1e3 / (n * C3S_LAYERS)
+    del graphs
+    us_layer = (res["check"] + (M_INTERVAL - 1) * res["reuse"]) / M_INTERVAL
     return {"workload": "config3: B=1, Hq=32, Hkv=8, D=128, bf16, ctx=131072 (8192 pages), "
                         f"pages split contiguously over {ws} GPU(s), lazy M=4, {C3S_LAYERS} layers",
-            "us_per_layer": ms * 1e3 / (n * C3S_LAYERS), "steps": n,
-            "launch": "eager: kernels plus host-side orchestration, NCCL all-gathers",
-            "stats_rank0": dict(pb.stats)}
+            "us_per_layer_lazy_check": res["check"], "us_per_layer_reuse": res["reuse"],
+            "us_per_layer": us_layer, "steps_per_kind": n,
+            "launch": ("CUDA graph per step kind (NCCL all-gathers inside)" if ok else
+                       "eager (graph capture of the collectives failed)"),
+            "stats_rank0_warmup": stats}
 
 
 C5_STEPS = 256

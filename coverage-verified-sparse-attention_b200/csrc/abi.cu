@@ -338,6 +338,22 @@ int cvsa_lse_merge(const float* o_d, const float* m_d, const float* l_d, const f
                      "lse_merge launch");
 }
 
+int cvsa_rank_merge(const float* parts, int32_t world, int64_t row_stride, int32_t batch,
+                    int32_t num_kv_heads, int32_t num_q_per_kv, int32_t head_dim,
+                    const uint8_t* need, void* out, int32_t out_dtype, void* stream) {
+  if (world <= 0 || batch < 0 || num_kv_heads <= 0 || num_q_per_kv <= 0 || head_dim <= 0)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if (!valid_dtype(out_dtype)) return fail(CVSA_ERR_INVALID, "out dtype unknown");
+  const int64_t rows = (int64_t)batch * num_kv_heads * num_q_per_kv;
+  if (row_stride < rows * (head_dim + 2)) return fail(CVSA_ERR_INVALID, "row_stride too small");
+  if (batch == 0) return CVSA_OK;
+  if (!parts || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  return cuda_status(launch_rank_merge(parts, world, row_stride, batch, num_kv_heads,
+                                       num_q_per_kv, head_dim, need, out, out_dtype,
+                                       (cudaStream_t)stream),
+                     "rank_merge launch");
+}
+
 int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
                        const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
                        const uint8_t* accept, const float* o_d, const float* m_d, const float* l_d,

@@ -167,6 +167,9 @@ cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_
                              const float* o_c, const float* m_c, const float* l_c,
                              const uint8_t* accept, int B, int hkv, int G, int D, void* out,
                              int out_dtype, cudaStream_t s);
+cudaError_t launch_rank_merge(const float* parts, int world, int64_t stride, int B, int hkv,
+                              int G, int D, const uint8_t* need, void* out, int out_dtype,
+                              cudaStream_t s);
 
 // ---- paged_kv.cu ----
 cudaError_t launch_paged_append(const KvView& kv, const void* k_new, const void* v_new, int B,

@@ -47,6 +47,44 @@ __global__ void lse_merge_kernel(const float* __restrict__ o_d, const float* __r
   }
 }
 
+// Fixed-order merge over the ranks of a page split: `world` exchanged rows of
+// `stride` floats, row r = [o_unnorm rows*D | m rows | l rows] of rank r.
+// M = max_r m_r, w_r = exp(m_r - M) (0 where m_r = -inf, M taken as 0 when
+// every m_r is -inf), out = sum_r w_r o_r / max(sum_r w_r l_r, 1e-6), summed
+// in rank order. One warp per query-head row; rows whose KV head has
+// need == 0 are left untouched when `need` is given.
+template <typename TO>
+__global__ void rank_merge_kernel(const float* __restrict__ parts, int world, int64_t stride,
+                                  int rows, int hq, int G, int D,
+                                  const uint8_t* __restrict__ need, TO* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  if (need != nullptr) {
+    const int b = row / hq;
+    if (need[b * (hq / G) + (row % hq) / G] == 0) return;
+  }
+  const int64_t m_off = (int64_t)rows * D;
+  const int64_t l_off = m_off + rows;
+  float M = neg_inf();
+  for (int r = 0; r < world; ++r) M = fmaxf(M, parts[r * stride + m_off + row]);
+  const float base = (M == neg_inf()) ? 0.f : M;
+  float L = 0.f;
+  for (int r = 0; r < world; ++r) {
+    const float mr = parts[r * stride + m_off + row];
+    if (mr != neg_inf()) L += parts[r * stride + l_off + row] * expf(mr - base);
+  }
+  const float denom = fmaxf(L, 1e-6f);
+  for (int d = lane; d < D; d += 32) {
+    float v = 0.f;
+    for (int r = 0; r < world; ++r) {
+      const float mr = parts[r * stride + m_off + row];
+      if (mr != neg_inf()) v += parts[r * stride + (int64_t)row * D + d] * expf(mr - base);
+    }
+    out[(int64_t)row * D + d] = Elem<TO>::from_f(v / denom);
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
@@ -70,6 +108,33 @@ cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_
     case CVSA_DTYPE_F32:
       lse_merge_kernel<<<grid, wpb * 32, 0, s>>>(o_d, m_d, l_d, o_c, m_c, l_c, accept, rows, hq,
                                                  G, D, (float*)out);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rank_merge(const float* parts, int world, int64_t stride, int B, int hkv,
+                              int G, int D, const uint8_t* need, void* out, int out_dtype,
+                              cudaStream_t s) {
+  const int rows = B * hkv * G;
+  if (rows == 0) return cudaSuccess;
+  const int wpb = 8;
+  const int grid = (rows + wpb - 1) / wpb;
+  const int hq = hkv * G;
+  switch (out_dtype) {
+    case CVSA_DTYPE_BF16:
+      rank_merge_kernel<<<grid, wpb * 32, 0, s>>>(parts, world, stride, rows, hq, G, D, need,
+                                                  (__nv_bfloat16*)out);
+      break;
+    case CVSA_DTYPE_F16:
+      rank_merge_kernel<<<grid, wpb * 32, 0, s>>>(parts, world, stride, rows, hq, G, D, need,
+                                                  (__half*)out);
+      break;
+    case CVSA_DTYPE_F32:
+      rank_merge_kernel<<<grid, wpb * 32, 0, s>>>(parts, world, stride, rows, hq, G, D, need,
+                                                  (float*)out);
       break;
     default:
       return cudaErrorInvalidValue;

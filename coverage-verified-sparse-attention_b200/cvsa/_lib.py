@@ -93,6 +93,7 @@ _SIGS = {
     "cvsa_sparse_decode": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P,
                             _P, _P, _I, _P, ctypes.c_size_t, _P], ctypes.c_int),
     "cvsa_lse_merge": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P], ctypes.c_int),
+    "cvsa_rank_merge": ([_P, _I, ctypes.c_int64, _I, _I, _I, _I, _P, _P, _I, _P], ctypes.c_int),
     "cvsa_recover_merge": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P,
                             _P, _P, _P, _I, _P, ctypes.c_size_t, _P], ctypes.c_int),
     "cvsa_step_workspace_size": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc),

@@ -78,6 +78,33 @@ def lse_merge(o_draft, m_draft, l_draft, o_comp, m_comp, l_comp, accept_mask,
     return out
 
 
+def rank_merge(parts: torch.Tensor, batch: int, num_kv_heads: int, num_q_per_kv: int,
+               head_dim: int, out: torch.Tensor, need: torch.Tensor = None) -> torch.Tensor:
+    """Fixed-order merge over ranks of page-split partials (cvsa_rank_merge).
+
+    parts [world, stride] float32: rank r's row holds o_unnorm [B, Hq, D],
+    m [B, Hq] and l [B, Hq] in that order. Writes the normalised output into
+    `out` [B, Hq, D] (its dtype); with `need` [B, H_kv] only the query heads
+    of KV heads where need is true. Returns `out`."""
+    dev = _lib.require_cuda(parts, out)
+    if parts.dtype != torch.float32 or parts.dim() != 2 or not parts.is_contiguous():
+        raise ValueError("parts must be a contiguous [world, stride] float32 tensor")
+    if not out.is_contiguous() or tuple(out.shape) != (batch, num_kv_heads * num_q_per_kv,
+                                                       head_dim):
+        raise ValueError("out must be a contiguous [B, Hq, D] tensor")
+    nd = None
+    if need is not None:
+        nd = need.to(torch.uint8).contiguous()
+        if nd.numel() != batch * num_kv_heads or nd.device != dev:
+            raise ValueError("need must be [B, H_kv] on the device of parts")
+    lib = _lib.load()
+    _lib.check(lib.cvsa_rank_merge(parts.data_ptr(), parts.shape[0], parts.shape[1], batch,
+                                   num_kv_heads, num_q_per_kv, head_dim, _lib.ptr(nd),
+                                   out.data_ptr(), _lib.dtype_code(out.dtype),
+                                   _lib.stream_ptr(dev)), "cvsa_rank_merge")
+    return out
+
+
 # Reference names.
 triton_compute_complement = compute_complement
 triton_check_coverage = check_coverage

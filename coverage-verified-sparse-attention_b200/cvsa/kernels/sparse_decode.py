@@ -16,7 +16,7 @@ from cvsa import _lib
 
 def _decode(q, k_cache, v_cache, block_tables, page_indices, n_per_head, context_lens,
             num_kv_heads, num_q_per_kv, block_size, want_unnorm: bool, want_out: bool,
-            out_dtype=None):
+            out_dtype=None, unnorm_out=None):
     dev = _lib.require_cuda(q, k_cache, v_cache, block_tables, page_indices, n_per_head,
                             context_lens)
     B, Hq, D = q.shape
@@ -32,7 +32,14 @@ def _decode(q, k_cache, v_cache, block_tables, page_indices, n_per_head, context
     qd = _lib.query_desc(q, block_tables, context_lens)
     lib = _lib.load()
     o = m = l = out = None
-    if want_unnorm:
+    if want_unnorm and unnorm_out is not None:
+        o, m, l = unnorm_out
+        for t, shape in ((o, (B, Hq, D)), (m, (B, Hq)), (l, (B, Hq))):
+            if (t.dtype != torch.float32 or tuple(t.shape) != shape or not t.is_contiguous()
+                    or t.device != dev):
+                raise ValueError("unnorm_out must be contiguous float32 (o, m, l) tensors "
+                                 "of shapes [B, Hq, D], [B, Hq], [B, Hq]")
+    elif want_unnorm:
         o = torch.empty((B, Hq, D), dtype=torch.float32, device=dev)
         m = torch.empty((B, Hq), dtype=torch.float32, device=dev)
         l = torch.empty((B, Hq), dtype=torch.float32, device=dev)
@@ -49,11 +56,15 @@ def _decode(q, k_cache, v_cache, block_tables, page_indices, n_per_head, context
 
 
 def sparse_decode_unnorm(q, k_cache, v_cache, block_tables, page_indices, n_per_head,
-                         context_lens, num_kv_heads, num_q_per_kv, block_size=64
+                         context_lens, num_kv_heads, num_q_per_kv, block_size=64, out=None
                          ) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """(O_unnorm [B,H_q,D], M [B,H_q], L [B,H_q]) float32 over the first n_per_head pages."""
+    """(O_unnorm [B,H_q,D], M [B,H_q], L [B,H_q]) float32 over the first n_per_head pages.
+
+    `out`, if given, is the (o, m, l) tensors to write (views into one
+    exchange buffer, for instance)."""
     o, m, l, _ = _decode(q, k_cache, v_cache, block_tables, page_indices, n_per_head,
-                         context_lens, num_kv_heads, num_q_per_kv, block_size, True, False)
+                         context_lens, num_kv_heads, num_q_per_kv, block_size, True, False,
+                         unnorm_out=out)
     return o, m, l
 
 

@@ -22,8 +22,17 @@ over the ranks:
      this is the merged result of backend.py:818-844) and a third all-gather
      merges them.
 Reuse steps need only exchange 2 (partials). A lazy check step gathers the
-cached selection's coverage sums first and continues as a reuse or a scoring
-step on every rank alike.
+cached selection's coverage sums first; every rank then takes the same
+decision from the same merged sums.
+
+No step reads a device value on the host: the lazy decision and the accept
+mask stay on the device and gate the work instead of branching around it. A
+lazy check step always runs the scoring step's launches and exchanges, and
+where the cached selection passed, its pages are the ones attended and kept;
+exact recovery always runs, attending no pages for heads that need none. The
+launches and exchanges of a step depend only on its host-known kind (first,
+check, reuse), so a layer's steps can be captured in CUDA graphs, NCCL
+all-gathers included, and every rank issues the same collectives.
 
 A step is a generator that yields each 1-D float32 tensor to all-gather and
 receives the [world, n] result; `run_step` drives it with torch.distributed,
@@ -72,13 +81,19 @@ def shard_sequence(k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: t
 
 
 class DeviceOps:
-    """The kernels of a page-split step: this package's CUDA ops."""
+    """The kernels of a page-split step: this package's CUDA ops.
+
+    score_pages, select_pages; decode_unnorm(..., out=(o, m, l)) writes its
+    partial into the given views of the exchange buffer; rank_merge(parts,
+    B, H_kv, G, D, out, need=None) merges the all-gathered partials of the
+    ranks in rank order into `out` (cvsa_rank_merge)."""
 
     def __init__(self):
-        from cvsa.kernels import page_scores, select, sparse_decode
+        from cvsa.kernels import coverage, page_scores, select, sparse_decode
         self.score_pages = page_scores.score_pages
         self.select_pages = select.select_pages
         self.decode_unnorm = sparse_decode.sparse_decode_unnorm
+        self.rank_merge = coverage.rank_merge
 
 
 def run_step(gen, allgather: Callable[[torch.Tensor], torch.Tensor]):
@@ -96,8 +111,13 @@ def dist_allgather(group=None) -> Callable[[torch.Tensor], torch.Tensor]:
 
     def ag(x: torch.Tensor) -> torch.Tensor:
         world = dist.get_world_size(group)
+        x = x.contiguous()
+        if x.is_cuda:
+            out = torch.empty((world,) + tuple(x.shape), dtype=x.dtype, device=x.device)
+            dist.all_gather_into_tensor(out, x, group=group)
+            return out
         outs = [torch.empty_like(x) for _ in range(world)]
-        dist.all_gather(outs, x.contiguous(), group=group)
+        dist.all_gather(outs, x, group=group)
         return torch.stack(outs)
     return ag
 
@@ -125,14 +145,6 @@ def _compact(mask: torch.Tensor, values: torch.Tensor, width: int, fill):
     return torch.where(m, v, torch.full_like(v, fill)), m.sum(-1).to(torch.int32)
 
 
-def _merge_partials(o, m, l):
-    """Fixed-order merge over ranks (dim 0) of unnormalised (o, m, l) partials."""
-    M = m.amax(0)
-    w = torch.where(torch.isinf(m) & (m < 0), torch.zeros_like(m),
-                    torch.exp(m - torch.where(torch.isinf(M), torch.zeros_like(M), M)))
-    return (o * w.unsqueeze(-1)).sum(0), M, (l * w).sum(0)
-
-
 class PageSplitBackend:
     """CVSA step over the pages a rank holds (see the module docstring).
 
@@ -140,6 +152,9 @@ class PageSplitBackend:
     context lengths (shard_sequence), plus the global context lengths and the
     global block-table width (the budget is int(W * budget_pct), backend.py:690).
     """
+
+    # device-side counters (the decisions never reach the host during a step)
+    _C_SCORING, _C_ACCEPT, _C_REJECT, _C_HEADS_ACC = range(4)
 
     def __init__(self, num_kv_heads: int, num_q_heads: int, head_dim: int, block_size: int,
                  rank: int, world: int, num_layers: int = 32, budget_pct: float = 0.10,
@@ -163,8 +178,20 @@ class PageSplitBackend:
         self.ops = ops or DeviceOps()
         self._cached: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
         self._step = 0
-        self.stats = dict(scoring_steps=0, coverage_checks=0, accept_steps=0, reject_steps=0,
-                          heads_accepted=0, heads_total=0)
+        self._host = dict(scoring_steps=0, coverage_checks=0, reject_steps=0, heads_total=0)
+        self._ctr: Optional[torch.Tensor] = None
+
+    @property
+    def stats(self) -> Dict[str, int]:
+        """scoring_steps, coverage_checks, accept_steps, reject_steps,
+        heads_accepted, heads_total (reads the device counters)."""
+        c = self._ctr.tolist() if self._ctr is not None else [0, 0, 0, 0]
+        h = self._host
+        return dict(scoring_steps=h["scoring_steps"] + c[self._C_SCORING],
+                    coverage_checks=h["coverage_checks"],
+                    accept_steps=c[self._C_ACCEPT],
+                    reject_steps=h["reject_steps"] + c[self._C_REJECT],
+                    heads_accepted=c[self._C_HEADS_ACC], heads_total=h["heads_total"])
 
     def step_done(self, layer_idx: int, num_layers: int):
         if layer_idx == num_layers - 1:
@@ -180,6 +207,11 @@ class PageSplitBackend:
                         global_context_lens, global_table_width)
         return run_step(gen, dist_allgather(self.process_group))
 
+    def _counters(self, dev) -> torch.Tensor:
+        if self._ctr is None:
+            self._ctr = torch.zeros(4, dtype=torch.int64, device=dev)
+        return self._ctr
+
     # ---- the step ---------------------------------------------------------
     def step(self, q, k, v, bt, cl, layer_idx, ctx_g, W_g):
         """Generator: yields tensors to all-gather, returns the output [B, Hq, D]."""
@@ -194,10 +226,12 @@ class PageSplitBackend:
         nv_g = (ctx_g.to(torch.int64).to(dev) + bs - 1) // bs
         lo, hi = page_range(nv_g, r, N)
         nv_r = hi - lo                                          # [B]
-        if B and int((nv_g // N).min()) < self.sink_pages + self.local_pages:
+        capturing = dev.type == "cuda" and torch.cuda.is_current_stream_capturing()
+        if B and not capturing and int((nv_g // N).min()) < self.sink_pages + self.local_pages:
             raise ValueError("every rank needs at least sink_pages + local_pages pages "
                              "of every sequence")
         cached = self._cached.get(layer_idx)
+        ctr = self._counters(dev)
         if self.lazy:
             check = self._step % self.check_interval == 0 or cached is None
         else:
@@ -221,41 +255,54 @@ class PageSplitBackend:
             lse_sel = torch.logsumexp(parts_sel, 0)
             return torch.exp(lse_sel - lse_all)
 
-        def draft_output(idx, n, extra=()):
-            o, m, l = attend(idx, n)
-            got = yield _pack(o, m, l, *extra)
-            parts = _unpack(got, (B, Hq, D), (B, Hq), (B, Hq), *[tuple(t.shape) for t in extra])
-            O, M, L = _merge_partials(parts[0], parts[1], parts[2])
-            return O, L, parts[3:]
+        n_part = B * Hq * (D + 2)
 
+        def exchange_partial(idx, n, extra=()):
+            """Attend (idx, n) straight into an exchange buffer ([o | m | l]
+            then `extra`), all-gather it; returns the [N, stride] rows and the
+            gathered extras."""
+            buf = torch.empty(n_part + sum(t.numel() for t in extra), dtype=torch.float32,
+                              device=dev)
+            o = buf[:B * Hq * D].view(B, Hq, D)
+            m = buf[B * Hq * D:B * Hq * (D + 1)].view(B, Hq)
+            l = buf[B * Hq * (D + 1):n_part].view(B, Hq)
+            self.ops.decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs, out=(o, m, l))
+            off = n_part
+            for t in extra:
+                buf[off:off + t.numel()].copy_(t.reshape(-1))
+                off += t.numel()
+            got = yield buf
+            return got, _unpack(got[:, n_part:], *[tuple(t.shape) for t in extra])
+
+        out = torch.empty((B, Hq, D), dtype=q.dtype, device=dev)
         if not scoring and not check:                           # reuse step
-            idx, n = cached
-            O, L, _ = yield from draft_output(idx, n)
-            return (O / L.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
+            got, _ = yield from exchange_partial(*cached)
+            return self.ops.rank_merge(got, B, H, G, D, out)
 
+        tau = torch.tensor(self.tau, dtype=torch.float32)
         scores = self.ops.score_pages(q, k, bt, cl, H, G, bs).float()   # [B, H, W_r]
+        reuse = None            # device bool: the cached selection passed the lazy gate
         if check:
             # lazy accounting of backend.py:420-465: every check counts; a layer
             # without a cached selection counts as a reject
-            self.stats["coverage_checks"] += 1
+            self._host["coverage_checks"] += 1
         if check and cached is None:
-            self.stats["reject_steps"] += 1
+            self._host["reject_steps"] += 1
         if check and cached is not None:
             sa, ss = lse_sums(scores, *cached)
             got = yield _pack(sa, ss)
             pa, ps = _unpack(got, (B, H), (B, H))
-            acc = coverage(pa, ps) >= torch.tensor(self.tau, dtype=torch.float32)
-            self.stats["heads_accepted"] += int(acc.sum())
-            self.stats["heads_total"] += acc.numel()
-            if bool(acc.all()):
-                self.stats["accept_steps"] += 1
-                idx, n = cached
-                O, L, _ = yield from draft_output(idx, n)
-                return (O / L.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
-            self.stats["reject_steps"] += 1
+            acc0 = coverage(pa, ps) >= tau
+            self._host["heads_total"] += acc0.numel()
+            reuse = acc0.all()
+            ctr[self._C_HEADS_ACC] += acc0.sum()
+            ctr[self._C_ACCEPT] += reuse
+            ctr[self._C_REJECT] += ~reuse
+            ctr[self._C_SCORING] += ~reuse
+        else:
+            self._host["scoring_steps"] += 1
 
-        # ---- scoring step ----
-        self.stats["scoring_steps"] += 1
+        # ---- scoring step (gated by `reuse` on a lazy check step) ----
         idx_l, n_l = self.ops.select_pages(scores, cl, bs, budget, sink_r, local_r)
         K = idx_l.shape[-1]
         pos = torch.arange(K, device=dev).view(1, 1, K)
@@ -287,23 +334,32 @@ class PageSplitBackend:
         all_idx = torch.cat([sink_idx, loc, tail], -1)
         all_mask = torch.cat([sink_idx >= 0, mine, tail >= 0], -1)
         idx_new, n_new = _compact(all_mask, all_idx, max_sel, 0)
-        idx_new = idx_new.to(torch.int32).contiguous()
+        idx_new = idx_new.to(torch.int32)
+        if reuse is not None:
+            idx_new = torch.where(reuse, cached[0], idx_new)
+            n_new = torch.where(reuse, cached[1], n_new)
+        idx_new, n_new = idx_new.contiguous(), n_new.contiguous()
         sa, ss = lse_sums(scores, idx_new, n_new)
-        O, L, (pa, ps) = yield from draft_output(idx_new, n_new, (sa, ss))
-        self._cached[layer_idx] = (idx_new, n_new)
-        acc = coverage(pa, ps) >= torch.tensor(self.tau, dtype=torch.float32)
+        got, (pa, ps) = yield from exchange_partial(idx_new, n_new, (sa, ss))
+        self.ops.rank_merge(got, B, H, G, D, out)
+        if cached is not None and cached[0].shape == idx_new.shape:
+            # in place: a captured reuse step keeps reading the same buffers
+            cached[0].copy_(idx_new)
+            cached[1].copy_(n_new)
+        else:
+            self._cached[layer_idx] = (idx_new, n_new)
+        acc = coverage(pa, ps) >= tau
         if not self.lazy:
-            self.stats["heads_accepted"] += int(acc.sum())
-            self.stats["heads_total"] += acc.numel()
-        out = O / L.clamp(min=1e-6).unsqueeze(-1)
-        if bool(acc.all()):
-            return out.to(q.dtype)
+            ctr[self._C_HEADS_ACC] += acc.sum()
+            self._host["heads_total"] += acc.numel()
         # exact recovery: rejected heads attend every valid page of the range
+        # and their merged result replaces the draft; heads that need none
+        # (accepted, or the cached selection passed the lazy gate) attend no
+        # pages and keep the draft
+        need = ~acc if reuse is None else ~acc & ~reuse
         Wr = scores.shape[-1]
         every = torch.arange(Wr, device=dev, dtype=torch.int32).view(1, 1, Wr).expand(B, H, Wr)
-        n_rec = torch.where(acc, torch.zeros_like(n_new), nv_r.view(B, 1).to(torch.int32)
-                            .expand(B, H))
-        O2, L2, _ = yield from draft_output(every.contiguous(), n_rec.contiguous())
-        out2 = O2 / L2.clamp(min=1e-6).unsqueeze(-1)
-        acc_q = acc.repeat_interleave(G, dim=1).unsqueeze(-1)
-        return torch.where(acc_q, out, out2).to(q.dtype)
+        n_rec = torch.where(need, nv_r.view(B, 1).to(torch.int32).expand(B, H),
+                            torch.zeros_like(n_new))
+        got, _ = yield from exchange_partial(every.contiguous(), n_rec.contiguous())
+        return self.ops.rank_merge(got, B, H, G, D, out, need=need)

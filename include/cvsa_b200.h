@@ -174,6 +174,22 @@ int cvsa_lse_merge(const float* o_d, const float* m_d, const float* l_d,
                    int32_t num_q_per_kv, int32_t head_dim, void* out, int32_t out_dtype,
                    void* stream);
 
+/* Fixed-order merge of the attention partials of a page-split step (the
+ * pages of every sequence split contiguously over `world` ranks; the
+ * reference has no multi-GPU path, this combines its per-rank
+ * triton_sparse_decode_unnorm partials, cvsa/kernels/sparse_decode.py:537-573,
+ * as cvsa/lse_merge.py:11-54 combines two). parts: `world` rows of
+ * row_stride floats in rank order (an all-gather's output); row r holds
+ * o_unnorm [batch, Hq, head_dim], then m [batch, Hq], then l [batch, Hq]
+ * (Hq = num_kv_heads * num_q_per_kv). With M = max_r m_r and
+ * w_r = exp(m_r - M) (0 where m_r = -inf): out = sum_r w_r o_r /
+ * max(sum_r w_r l_r, 1e-6), summed in rank order, in out_dtype. If need
+ * ([batch, num_kv_heads] uint8) is given, only the query heads of KV heads
+ * with need != 0 are written. */
+int cvsa_rank_merge(const float* parts, int32_t world, int64_t row_stride, int32_t batch,
+                    int32_t num_kv_heads, int32_t num_q_per_kv, int32_t head_dim,
+                    const uint8_t* need, void* out, int32_t out_dtype, void* stream);
+
 /* Fused exact recovery: for heads with accept == 0, attend to the valid pages
  * NOT in the selection (skipped through a selection bitmap, never
  * materialised as an index list) and LSE-merge that complement partial with

@@ -74,6 +74,15 @@ def test_validation_rejects_before_any_cuda_call():
     cfg.mode = 7
     io = _lib.StepIO(16, 16, 28, 0, 16, None, None, None, None, None, None)
     assert lib.cvsa_decode_step(qd, kv, cfg, io, 256, 1 << 30, None) == _lib.ERR_INVALID
+    # page-split rank merge: no ranks, rows shorter than [o | m | l], unknown dtype
+    bf16 = _lib.DTYPE_BF16
+    assert lib.cvsa_rank_merge(16, 0, 2 * 32 * 130, 2, 8, 4, 128, None, 16, bf16, None) \
+        == _lib.ERR_INVALID
+    assert lib.cvsa_rank_merge(16, 2, 2 * 32 * 130 - 1, 2, 8, 4, 128, None, 16, bf16, None) \
+        == _lib.ERR_INVALID
+    assert b"row_stride" in lib.cvsa_last_error()
+    assert lib.cvsa_rank_merge(16, 2, 2 * 32 * 130, 2, 8, 4, 128, None, 16, 9, None) \
+        == _lib.ERR_INVALID
 
 
 def test_status_codes_map_to_reference_exceptions():

@@ -262,3 +262,40 @@ def test_lse_merge_vs_reference_formula(cuda):
                                     torch.bfloat16)
         # one bf16 rounding of the same fp32 value: within the bf16 bar
         assert ((out16.float().cpu() - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
+
+
+@pytest.mark.parametrize("world", [1, 3, 8])
+def test_rank_merge_vs_fp32_formula(cuda, world):
+    """cvsa_rank_merge against the fp32 LSE merge over ranks (rank order),
+    with empty partials (m = -inf, l = 0, o = 0) on some ranks and rows empty
+    on every rank; `need` leaves the other heads' rows untouched."""
+    from cvsa.kernels.coverage import rank_merge
+    g = torch.Generator().manual_seed(world)
+    B, Hkv, G, D = 3, 4, 4, 128
+    Hq = Hkv * G
+    o = torch.randn(world, B, Hq, D, generator=g)
+    m = torch.randn(world, B, Hq, generator=g) * 3
+    l = torch.rand(world, B, Hq, generator=g) + 0.1
+    empty = torch.rand(world, B, Hq, generator=g) < 0.3
+    empty[:, 0, 0] = True                                   # a row empty on every rank
+    o[empty.unsqueeze(-1).expand_as(o)] = 0
+    m[empty] = float("-inf")
+    l[empty] = 0
+    parts = torch.cat([o.reshape(world, -1), m.reshape(world, -1), l.reshape(world, -1),
+                       torch.randn(world, 7, generator=g)], 1).contiguous()
+    M = m.amax(0)
+    w = torch.where(empty, torch.zeros_like(m),
+                    torch.exp(m - torch.where(torch.isinf(M), torch.zeros_like(M), M)))
+    ref = (o * w.unsqueeze(-1)).sum(0) / (l * w).sum(0).clamp(min=1e-6).unsqueeze(-1)
+    out = rank_merge(parts.to(cuda), B, Hkv, G, D, torch.empty(B, Hq, D, device=cuda))
+    assert (out.cpu() - ref).abs().max() < 1e-5
+    assert (out[0, 0] == 0).all()
+    out16 = rank_merge(parts.to(cuda), B, Hkv, G, D,
+                       torch.empty(B, Hq, D, dtype=torch.bfloat16, device=cuda))
+    assert ((out16.float().cpu() - ref).abs() <= 2e-2 + 1e-2 * ref.abs()).all()
+    need = torch.rand(B, Hkv, generator=g) < 0.5
+    keep = torch.full((B, Hq, D), 7.0)
+    got = rank_merge(parts.to(cuda), B, Hkv, G, D, keep.clone().to(cuda), need=need.to(cuda))
+    nq = need.repeat_interleave(G, dim=1).unsqueeze(-1)
+    want = torch.where(nq, ref, keep)
+    assert (got.cpu() - want).abs().max() < 1e-5

@@ -36,6 +36,11 @@ def _lockstep(gens):
         xs = outs
 
 
+def _check_close(out, ref, step):
+    a, b = out.float(), ref.float()
+    assert ((a - b).abs() <= 2e-2 + 1e-2 * b.abs()).all(), (step, float((a - b).abs().max()))
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_page_split_matches_one_gpu(cuda, world):
     wl = synthetic.small(seed=31, B=2, Hq=32, Hkv=8, D=128, ctx=(9000, 4100), heavy_alpha=4.0,
@@ -58,8 +63,7 @@ def test_page_split_matches_one_gpu(cuda, world):
         outs = _lockstep([pb.step(q, k, v, bt, cl, 0, d.context_lens, d.block_tables.shape[1])
                           for pb, k, v, bt, cl, _ in ranks])
         for out in outs:
-            a, b = out.float(), ref.float()
-            assert ((a - b).abs() <= 2e-2 + 1e-2 * b.abs()).all(), (step, float((a - b).abs().max()))
+            _check_close(out, ref, step)
         fi, fn = full.cached_selection(0)
         for b in range(2):
             for h in range(8):
@@ -71,3 +75,67 @@ def test_page_split_matches_one_gpu(cuda, world):
         full.step_done(0, 1)
         for pb, *_ in ranks:
             pb.step_done(0, 1)
+
+
+def test_page_split_steps_replay_as_graphs(cuda):
+    """The check and reuse steps of two lockstep ranks, captured once each as
+    CUDA graphs (no device value is read on the host inside a step), replayed
+    over a lazy schedule with fresh queries copied into the captured input:
+    every replay must match CVSABackend's step, and the in-place cached
+    selections its cached selection."""
+    world = 2
+    wl = synthetic.small(seed=32, B=2, Hq=32, Hkv=8, D=128, ctx=(8000, 5000), heavy_alpha=4.0,
+                         budget_pct=0.05)
+    d = wl.to(cuda)
+    kw = dict(num_layers=1, budget_pct=0.05, coverage_threshold=0.9, lazy=True,
+              check_interval=2, sink_pages=1, local_pages=2)
+    full = CVSABackend(8, 32, 128, 16, **kw)
+    nv = (wl.context_lens.long() + 15) // 16
+    ranks = []
+    for r in range(world):
+        k, v, bt, cl = shard_sequence(d.k_cache, d.v_cache, d.block_tables, d.context_lens,
+                                      r, world, 16)
+        ranks.append((PageSplitBackend(8, 32, 128, 16, r, world, **kw), k, v, bt, cl,
+                      page_range(nv, r, world)))
+    qbuf = d.q.clone()
+    W = d.block_tables.shape[1]
+
+    def lockstep():
+        return _lockstep([pb.step(qbuf, k, v, bt, cl, 0, d.context_lens, W)
+                          for pb, k, v, bt, cl, _ in ranks])
+
+    g = torch.Generator(device="cpu").manual_seed(9)
+    queries = [(wl.q.float() + 0.6 * torch.randn(wl.q.shape, generator=g)).to(wl.q.dtype)
+               for _ in range(8)]
+    # step 0 eager: no cached selection yet
+    qbuf.copy_(queries[0].to(cuda))
+    outs0 = lockstep()
+    ref = full(qbuf, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+    for out in outs0:
+        _check_close(out, ref, 0)
+    full.step_done(0, 1)
+    graphs, static = {}, {}
+    for kind, step_idx in (("check", 0), ("reuse", 1)):
+        for pb, *_ in ranks:
+            pb._step = step_idx
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            static[kind] = lockstep()
+        graphs[kind] = gr
+    for step in range(1, 8):
+        kind = "check" if step % 2 == 0 else "reuse"
+        qbuf.copy_(queries[step].to(cuda))
+        graphs[kind].replay()
+        ref = full(qbuf, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        torch.cuda.synchronize()
+        for out in static[kind]:
+            _check_close(out, ref, step)
+        fi, fn = full.cached_selection(0)
+        for b in range(2):
+            for h in range(8):
+                union = []
+                for pb, *_rest, (lo, hi) in ranks:
+                    li, ln = pb.cached_selection(0)
+                    union += [p + int(lo[b]) for p in li[b, h, :int(ln[b, h])].tolist()]
+                assert union == fi[b, h, :int(fn[b, h])].tolist(), (step, b, h)
+        full.step_done(0, 1)

@@ -26,13 +26,40 @@ from oracle import cvsa_ref as R
 
 
 class OracleOps:
-    """The oracle's restatement of the three kernels a page-split step runs."""
+    """The oracle's restatement of the kernels a page-split step runs."""
     score_pages = staticmethod(R.score_pages)
-    decode_unnorm = staticmethod(R.sparse_decode_unnorm)
 
     @staticmethod
     def select_pages(scores, cl, bs, budget, sink, local):
         return R.select_pages(scores, cl, bs, budget, sink, local)
+
+    @staticmethod
+    def decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs, out=None):
+        o, m, l = R.sparse_decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs)
+        if out is None:
+            return o, m, l
+        for dst, src in zip(out, (o, m, l)):
+            dst.copy_(src)
+        return out
+
+    @staticmethod
+    def rank_merge(parts, B, H, G, D, out, need=None):
+        """The LSE merge of cvsa/lse_merge.py:11-54 taken over the ranks
+        (dim 0), in rank order, normalised by max(l, 1e-6)."""
+        Hq = H * G
+        o = parts[:, :B * Hq * D].reshape(-1, B, Hq, D)
+        m = parts[:, B * Hq * D:B * Hq * (D + 1)].reshape(-1, B, Hq)
+        l = parts[:, B * Hq * (D + 1):B * Hq * (D + 2)].reshape(-1, B, Hq)
+        M = m.amax(0)
+        w = torch.where(torch.isinf(m) & (m < 0), torch.zeros_like(m),
+                        torch.exp(m - torch.where(torch.isinf(M), torch.zeros_like(M), M)))
+        res = (o * w.unsqueeze(-1)).sum(0) / (l * w).sum(0).clamp(min=1e-6).unsqueeze(-1)
+        if need is None:
+            out.copy_(res)
+        else:
+            nq = need.repeat_interleave(G, dim=1).unsqueeze(-1)
+            out.copy_(torch.where(nq, res.to(out.dtype), out))
+        return out
 
 
 def _free_port() -> int:
