@@ -303,23 +303,23 @@ class PageSplitBackend:
             self._host["scoring_steps"] += 1
 
         # ---- scoring step (gated by `reuse` on a lazy check step) ----
-        idx_l, n_l = self.ops.select_pages(scores, cl, bs, budget, sink_r, local_r)
-        K = idx_l.shape[-1]
-        pos = torch.arange(K, device=dev).view(1, 1, K)
-        valid = pos < n_l.unsqueeze(-1)
+        # proposals: this rank's selection at the common width max_sel, page
+        # order, forced and unused slots at -inf (never chosen over a page)
+        idx_l, n_l = self.ops.select_pages(scores, cl, bs, budget, sink_r, local_r,
+                                           max_sel=max_sel)
+        pos = torch.arange(max_sel, device=dev).view(1, 1, max_sel)
         il = idx_l.long()
         forced = (il < sink_r) | (il >= (nv_r.view(B, 1, 1) - local_r))
-        cand = valid & ~forced
-        cand_s = torch.where(cand, torch.gather(scores, -1, il.clamp(min=0)),
-                             torch.full(il.shape, NEG_INF, device=dev))
-        cand_g = (il + lo.view(B, 1, 1)).to(torch.float32)
-        cs, _ = _compact(cand, cand_s, budget, NEG_INF)
-        cg, _ = _compact(cand, cand_g, budget, -1.0)
-        got = yield _pack(cs, cg)                               # [N, 2 * B * H * budget]
-        all_s, all_g = _unpack(got, (B, H, budget), (B, H, budget))
-        tab_s = all_s.permute(1, 2, 0, 3).reshape(B, H, N * budget).contiguous()
-        tab_g = all_g.permute(1, 2, 0, 3).reshape(B, H, N * budget)
-        tab_len = torch.full((B,), N * budget * bs, dtype=torch.int32, device=dev)
+        cand = (pos < n_l.unsqueeze(-1)) & ~forced
+        cs = torch.where(cand, torch.gather(scores, -1, il.clamp(min=0)),
+                         torch.full(il.shape, NEG_INF, device=dev))
+        cg = (il + lo.view(B, 1, 1)).to(torch.float32)
+        got = yield _pack(cs, cg)                               # [N, 2 * B * H * max_sel]
+        all_s, all_g = _unpack(got, (B, H, max_sel), (B, H, max_sel))
+        # rank order then page order: table position order is global page order
+        tab_s = all_s.permute(1, 2, 0, 3).reshape(B, H, N * max_sel).contiguous()
+        tab_g = all_g.permute(1, 2, 0, 3).reshape(B, H, N * max_sel)
+        tab_len = torch.full((B,), N * max_sel * bs, dtype=torch.int32, device=dev)
         tpos, tn = self.ops.select_pages(tab_s, tab_len, bs, budget, 0, 0)
         tm = torch.arange(tpos.shape[-1], device=dev).view(1, 1, -1) < tn.unsqueeze(-1)
         sel_g = torch.gather(tab_g, -1, tpos.long().clamp(min=0))

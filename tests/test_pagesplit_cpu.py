@@ -30,8 +30,11 @@ class OracleOps:
     score_pages = staticmethod(R.score_pages)
 
     @staticmethod
-    def select_pages(scores, cl, bs, budget, sink, local):
-        return R.select_pages(scores, cl, bs, budget, sink, local)
+    def select_pages(scores, cl, bs, budget, sink, local, max_sel=None):
+        idx, n = R.select_pages(scores, cl, bs, budget, sink, local)
+        if max_sel is not None and idx.shape[-1] < max_sel:
+            idx = torch.nn.functional.pad(idx, (0, max_sel - idx.shape[-1]))
+        return idx, n
 
     @staticmethod
     def decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs, out=None):
