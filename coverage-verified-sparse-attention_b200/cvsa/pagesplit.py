@@ -223,13 +223,6 @@ class PageSplitBackend:
         sink_r = self.sink_pages if r == 0 else 0
         local_r = self.local_pages if r == N - 1 else 0
         max_sel = budget + self.sink_pages + self.local_pages
-        nv_g = (ctx_g.to(torch.int64).to(dev) + bs - 1) // bs
-        lo, hi = page_range(nv_g, r, N)
-        nv_r = hi - lo                                          # [B]
-        capturing = dev.type == "cuda" and torch.cuda.is_current_stream_capturing()
-        if B and not capturing and int((nv_g // N).min()) < self.sink_pages + self.local_pages:
-            raise ValueError("every rank needs at least sink_pages + local_pages pages "
-                             "of every sequence")
         cached = self._cached.get(layer_idx)
         ctr = self._counters(dev)
         if self.lazy:
@@ -242,13 +235,12 @@ class PageSplitBackend:
         def attend(idx, n):
             return self.ops.decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs)
 
-        def lse_sums(scores, idx, n):
-            s_all = torch.logsumexp(scores, -1)
+        def lse_sel(scores, idx, n):
+            """log-sum-exp of the scores of the first n entries of idx."""
             K = idx.shape[-1]
             mask = torch.arange(K, device=dev).view(1, 1, K) < n.unsqueeze(-1)
             sel = torch.gather(scores, -1, idx.long().clamp(min=0))
-            sel = torch.where(mask, sel, torch.full_like(sel, NEG_INF))
-            return s_all, torch.logsumexp(sel, -1)
+            return torch.logsumexp(sel.masked_fill(~mask, NEG_INF), -1)
 
         def coverage(parts_all, parts_sel):
             lse_all = torch.logsumexp(parts_all, 0)
@@ -279,8 +271,18 @@ class PageSplitBackend:
             got, _ = yield from exchange_partial(*cached)
             return self.ops.rank_merge(got, B, H, G, D, out)
 
+        # the rank's page range of every sequence (only scoring and check
+        # steps need it)
+        nv_g = (ctx_g.to(device=dev, dtype=torch.int64) + bs - 1) // bs
+        lo, hi = page_range(nv_g, r, N)
+        nv_r = hi - lo                                          # [B]
+        capturing = dev.type == "cuda" and torch.cuda.is_current_stream_capturing()
+        if B and not capturing and int((nv_g // N).min()) < self.sink_pages + self.local_pages:
+            raise ValueError("every rank needs at least sink_pages + local_pages pages "
+                             "of every sequence")
         tau = torch.tensor(self.tau, dtype=torch.float32)
-        scores = self.ops.score_pages(q, k, bt, cl, H, G, bs).float()   # [B, H, W_r]
+        scores = self.ops.score_pages(q, k, bt, cl, H, G, bs)          # [B, H, W_r] f32
+        s_all = torch.logsumexp(scores, -1)                     # [B, H], every valid page
         reuse = None            # device bool: the cached selection passed the lazy gate
         if check:
             # lazy accounting of backend.py:420-465: every check counts; a layer
@@ -289,8 +291,7 @@ class PageSplitBackend:
         if check and cached is None:
             self._host["reject_steps"] += 1
         if check and cached is not None:
-            sa, ss = lse_sums(scores, *cached)
-            got = yield _pack(sa, ss)
+            got = yield _pack(s_all, lse_sel(scores, *cached))
             pa, ps = _unpack(got, (B, H), (B, H))
             acc0 = coverage(pa, ps) >= tau
             self._host["heads_total"] += acc0.numel()
@@ -339,8 +340,8 @@ class PageSplitBackend:
             idx_new = torch.where(reuse, cached[0], idx_new)
             n_new = torch.where(reuse, cached[1], n_new)
         idx_new, n_new = idx_new.contiguous(), n_new.contiguous()
-        sa, ss = lse_sums(scores, idx_new, n_new)
-        got, (pa, ps) = yield from exchange_partial(idx_new, n_new, (sa, ss))
+        got, (pa, ps) = yield from exchange_partial(idx_new, n_new,
+                                                    (s_all, lse_sel(scores, idx_new, n_new)))
         self.ops.rank_merge(got, B, H, G, D, out)
         if cached is not None and cached[0].shape == idx_new.shape:
             # in place: a captured reuse step keeps reading the same buffers
