@@ -312,23 +312,20 @@ class PageSplitBackend:
         il = idx_l.long()
         forced = (il < sink_r) | (il >= (nv_r.view(B, 1, 1) - local_r))
         cand = (pos < n_l.unsqueeze(-1)) & ~forced
-        cs = torch.where(cand, torch.gather(scores, -1, il.clamp(min=0)),
-                         torch.full(il.shape, NEG_INF, device=dev))
-        cg = (il + lo.view(B, 1, 1)).to(torch.float32)
-        got = yield _pack(cs, cg)                               # [N, 2 * B * H * max_sel]
-        all_s, all_g = _unpack(got, (B, H, max_sel), (B, H, max_sel))
-        # rank order then page order: table position order is global page order
-        tab_s = all_s.permute(1, 2, 0, 3).reshape(B, H, N * max_sel).contiguous()
-        tab_g = all_g.permute(1, 2, 0, 3).reshape(B, H, N * max_sel)
+        cs = torch.gather(scores, -1, il.clamp(min=0)).masked_fill(~cand, NEG_INF)
+        got = yield cs.reshape(-1)                              # [N, B * H * max_sel]
+        # rank order then slot order: table position order is global page order
+        tab_s = got.view(N, B, H, max_sel).permute(1, 2, 0, 3).reshape(B, H, N * max_sel)
+        tab_s = tab_s.contiguous()
         tab_len = torch.full((B,), N * max_sel * bs, dtype=torch.int32, device=dev)
         tpos, tn = self.ops.select_pages(tab_s, tab_len, bs, budget, 0, 0)
-        tm = torch.arange(tpos.shape[-1], device=dev).view(1, 1, -1) < tn.unsqueeze(-1)
-        sel_g = torch.gather(tab_g, -1, tpos.long().clamp(min=0))
-        sel_g = torch.where(tm & torch.isfinite(torch.gather(tab_s, -1, tpos.long().clamp(min=0))),
-                            sel_g, torch.full_like(sel_g, -1.0)).long()
-        # my pages of the global selection, with my forced pages, ascending
-        mine = (sel_g >= lo.view(B, 1, 1)) & (sel_g < hi.view(B, 1, 1))
-        loc = sel_g - lo.view(B, 1, 1)
+        tp = tpos.long().clamp(min=0)
+        chosen = (torch.arange(tp.shape[-1], device=dev).view(1, 1, -1) < tn.unsqueeze(-1)) \
+            & torch.isfinite(torch.gather(tab_s, -1, tp))
+        # my pages of the global selection (a position of my block maps to the
+        # page in that slot of my proposals), with my forced pages, ascending
+        mine = chosen & (tp // max_sel == r)
+        loc = torch.gather(il, -1, tp % max_sel)
         sink_idx = torch.arange(sink_r, device=dev).view(1, 1, -1).expand(B, H, sink_r)
         tail = (nv_r.view(B, 1, 1) - local_r + torch.arange(local_r, device=dev).view(1, 1, -1)
                 ).expand(B, H, local_r)
