@@ -354,6 +354,30 @@ int cvsa_rank_merge(const float* parts, int32_t world, int64_t row_stride, int32
                      "rank_merge launch");
 }
 
+int cvsa_page_lse(const float* page_scores, int32_t rows, int32_t max_pages,
+                  const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
+                  float* lse_all, float* lse_sel, void* stream) {
+  if (rows < 0 || max_pages <= 0 || max_sel <= 0) return fail(CVSA_ERR_INVALID, "bad shape");
+  if (rows == 0) return CVSA_OK;
+  if (!page_scores || !page_indices || !n_per_head || !lse_all || !lse_sel)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  return cuda_status(launch_page_lse(page_scores, rows, max_pages, page_indices, max_sel,
+                                     n_per_head, lse_all, lse_sel, (cudaStream_t)stream),
+                     "page_lse launch");
+}
+
+int cvsa_rank_accept(const float* parts, int32_t world, int64_t row_stride, int64_t off_all,
+                     int64_t off_sel, int32_t rows, float tau, uint8_t* accept, void* stream) {
+  if (world <= 0 || rows < 0 || off_all < 0 || off_sel < 0 || off_all + rows > row_stride ||
+      off_sel + rows > row_stride)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if (rows == 0) return CVSA_OK;
+  if (!parts || !accept) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  return cuda_status(launch_rank_accept(parts, world, row_stride, off_all, off_sel, rows, tau,
+                                        accept, (cudaStream_t)stream),
+                     "rank_accept launch");
+}
+
 int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
                        const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
                        const uint8_t* accept, const float* o_d, const float* m_d, const float* l_d,

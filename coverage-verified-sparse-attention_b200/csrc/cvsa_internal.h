@@ -170,6 +170,12 @@ cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_
 cudaError_t launch_rank_merge(const float* parts, int world, int64_t stride, int B, int hkv,
                               int G, int D, const uint8_t* need, void* out, int out_dtype,
                               cudaStream_t s);
+cudaError_t launch_page_lse(const float* scores, int rows, int W, const int32_t* idx,
+                            int max_sel, const int32_t* n, float* lse_all, float* lse_sel,
+                            cudaStream_t s);
+cudaError_t launch_rank_accept(const float* parts, int world, int64_t stride, int64_t off_all,
+                               int64_t off_sel, int rows, float tau, uint8_t* accept,
+                               cudaStream_t s);
 
 // ---- paged_kv.cu ----
 cudaError_t launch_paged_append(const KvView& kv, const void* k_new, const void* v_new, int B,

@@ -85,6 +85,76 @@ __global__ void rank_merge_kernel(const float* __restrict__ parts, int world, in
   }
 }
 
+// Per (sequence, KV head) row of page scores: log-sum-exp over the W entries
+// (-inf entries carry no mass) and over the first n entries of the row's
+// selection (entries outside [0, W) are skipped); -inf when empty. One warp
+// per row, an online (max, sum) per lane combined across the warp.
+__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
+  if (x == neg_inf()) return;
+  if (x > m) {
+    s = s * expf(m - x) + 1.f;
+    m = x;
+  } else {
+    s += expf(x - m);
+  }
+}
+
+__device__ __forceinline__ float lse_warp(float m, float s) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+    const float so = __shfl_xor_sync(0xffffffffu, s, o);
+    const float M = fmaxf(m, mo);
+    if (M == neg_inf()) continue;
+    s = (m == neg_inf() ? 0.f : s * expf(m - M)) + (mo == neg_inf() ? 0.f : so * expf(mo - M));
+    m = M;
+  }
+  return m == neg_inf() ? neg_inf() : m + logf(s);
+}
+
+__global__ void page_lse_kernel(const float* __restrict__ scores, int rows, int W,
+                                const int32_t* __restrict__ idx, int max_sel,
+                                const int32_t* __restrict__ n, float* __restrict__ lse_all,
+                                float* __restrict__ lse_sel) {
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const float* sr = scores + (int64_t)row * W;
+  float m = neg_inf(), s = 0.f;
+  for (int p = lane; p < W; p += 32) lse_push(m, s, sr[p]);
+  const float all = lse_warp(m, s);
+  m = neg_inf();
+  s = 0.f;
+  const int cnt = min(n[row], max_sel);
+  for (int j = lane; j < cnt; j += 32) {
+    const int p = idx[(int64_t)row * max_sel + j];
+    if (p >= 0 && p < W) lse_push(m, s, sr[p]);
+  }
+  const float sel = lse_warp(m, s);
+  if (lane == 0) {
+    lse_all[row] = all;
+    lse_sel[row] = sel;
+  }
+}
+
+// The coverage gate over the ranks of a page split: row i's coverage is
+// exp(LSE_r sel_r - LSE_r all_r) over the gathered per-rank log-sum-exps
+// (rank r's values at parts[r * stride + off_all + i] and off_sel + i);
+// accept[i] = coverage >= tau.
+__global__ void rank_accept_kernel(const float* __restrict__ parts, int world, int64_t stride,
+                                   int64_t off_all, int64_t off_sel, int rows, float tau,
+                                   uint8_t* __restrict__ accept) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows) return;
+  float ma = neg_inf(), sa = 0.f, ms = neg_inf(), ss = 0.f;
+  for (int r = 0; r < world; ++r) {
+    lse_push(ma, sa, parts[r * stride + off_all + i]);
+    lse_push(ms, ss, parts[r * stride + off_sel + i]);
+  }
+  const float la = ma == neg_inf() ? neg_inf() : ma + logf(sa);
+  const float ls = ms == neg_inf() ? neg_inf() : ms + logf(ss);
+  accept[i] = expf(ls - la) >= tau ? 1 : 0;
+}
+
 }  // namespace
 
 cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
@@ -139,6 +209,25 @@ cudaError_t launch_rank_merge(const float* parts, int world, int64_t stride, int
     default:
       return cudaErrorInvalidValue;
   }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_page_lse(const float* scores, int rows, int W, const int32_t* idx,
+                            int max_sel, const int32_t* n, float* lse_all, float* lse_sel,
+                            cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  const int wpb = 8;
+  page_lse_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, s>>>(scores, rows, W, idx, max_sel, n,
+                                                              lse_all, lse_sel);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rank_accept(const float* parts, int world, int64_t stride, int64_t off_all,
+                               int64_t off_sel, int rows, float tau, uint8_t* accept,
+                               cudaStream_t s) {
+  if (rows == 0) return cudaSuccess;
+  rank_accept_kernel<<<(rows + 127) / 128, 128, 0, s>>>(parts, world, stride, off_all, off_sel,
+                                                         rows, tau, accept);
   return cudaGetLastError();
 }
 

@@ -93,6 +93,9 @@ _SIGS = {
     "cvsa_sparse_decode": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P,
                             _P, _P, _I, _P, ctypes.c_size_t, _P], ctypes.c_int),
     "cvsa_lse_merge": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P], ctypes.c_int),
+    "cvsa_page_lse": ([_P, _I, _I, _P, _I, _P, _P, _P, _P], ctypes.c_int),
+    "cvsa_rank_accept": ([_P, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _I,
+                          ctypes.c_float, _P, _P], ctypes.c_int),
     "cvsa_rank_merge": ([_P, _I, ctypes.c_int64, _I, _I, _I, _I, _P, _P, _I, _P], ctypes.c_int),
     "cvsa_recover_merge": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P,
                             _P, _P, _P, _I, _P, ctypes.c_size_t, _P], ctypes.c_int),

@@ -105,6 +105,40 @@ def rank_merge(parts: torch.Tensor, batch: int, num_kv_heads: int, num_q_per_kv:
     return out
 
 
+def page_lse(page_scores: torch.Tensor, page_indices: torch.Tensor, n_per_head: torch.Tensor):
+    """(lse_all, lse_sel) [B, H_kv] float32 of page scores [B, H_kv, W]: the
+    log-sum-exp over every page and over the first n_per_head selected pages
+    (cvsa_page_lse; -inf when empty)."""
+    dev = _lib.require_cuda(page_scores, page_indices, n_per_head)
+    B, H, W = page_scores.shape
+    ps = page_scores.float().contiguous()
+    pi = page_indices.to(torch.int32).reshape(B, H, -1).contiguous()
+    nph = n_per_head.to(torch.int32).reshape(B, H).contiguous()
+    lse_all = torch.empty((B, H), dtype=torch.float32, device=dev)
+    lse_sel = torch.empty((B, H), dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.cvsa_page_lse(ps.data_ptr(), B * H, max(W, 1), pi.data_ptr(),
+                                 max(pi.shape[2], 1), nph.data_ptr(), lse_all.data_ptr(),
+                                 lse_sel.data_ptr(), _lib.stream_ptr(dev)), "cvsa_page_lse")
+    return lse_all, lse_sel
+
+
+def rank_accept(parts: torch.Tensor, off_all: int, off_sel: int, rows: int,
+                tau: float) -> torch.Tensor:
+    """accept [rows] bool of the coverage gate over ranks (cvsa_rank_accept):
+    parts [world, stride] float32 holds each rank's lse_all at off_all and
+    lse_sel at off_sel."""
+    dev = _lib.require_cuda(parts)
+    if parts.dtype != torch.float32 or parts.dim() != 2 or not parts.is_contiguous():
+        raise ValueError("parts must be a contiguous [world, stride] float32 tensor")
+    acc = torch.empty(rows, dtype=torch.uint8, device=dev)
+    lib = _lib.load()
+    _lib.check(lib.cvsa_rank_accept(parts.data_ptr(), parts.shape[0], parts.shape[1], off_all,
+                                    off_sel, rows, float(tau), acc.data_ptr(),
+                                    _lib.stream_ptr(dev)), "cvsa_rank_accept")
+    return acc.bool()
+
+
 # Reference names.
 triton_compute_complement = compute_complement
 triton_check_coverage = check_coverage

@@ -86,7 +86,10 @@ class DeviceOps:
     score_pages, select_pages; decode_unnorm(..., out=(o, m, l)) writes its
     partial into the given views of the exchange buffer; rank_merge(parts,
     B, H_kv, G, D, out, need=None) merges the all-gathered partials of the
-    ranks in rank order into `out` (cvsa_rank_merge)."""
+    ranks in rank order into `out` (cvsa_rank_merge); page_lse(scores, idx,
+    n) gives a rank's two coverage log-sum-exps (cvsa_page_lse) and
+    rank_accept(parts, off_all, off_sel, rows, tau) the gate over the
+    gathered ones (cvsa_rank_accept)."""
 
     def __init__(self):
         from cvsa.kernels import coverage, page_scores, select, sparse_decode
@@ -94,6 +97,8 @@ class DeviceOps:
         self.select_pages = select.select_pages
         self.decode_unnorm = sparse_decode.sparse_decode_unnorm
         self.rank_merge = coverage.rank_merge
+        self.page_lse = coverage.page_lse
+        self.rank_accept = coverage.rank_accept
 
 
 def run_step(gen, allgather: Callable[[torch.Tensor], torch.Tensor]):
@@ -235,18 +240,6 @@ class PageSplitBackend:
         def attend(idx, n):
             return self.ops.decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs)
 
-        def lse_sel(scores, idx, n):
-            """log-sum-exp of the scores of the first n entries of idx."""
-            K = idx.shape[-1]
-            mask = torch.arange(K, device=dev).view(1, 1, K) < n.unsqueeze(-1)
-            sel = torch.gather(scores, -1, idx.long().clamp(min=0))
-            return torch.logsumexp(sel.masked_fill(~mask, NEG_INF), -1)
-
-        def coverage(parts_all, parts_sel):
-            lse_all = torch.logsumexp(parts_all, 0)
-            lse_sel = torch.logsumexp(parts_sel, 0)
-            return torch.exp(lse_sel - lse_all)
-
         n_part = B * Hq * (D + 2)
 
         def exchange_partial(idx, n, extra=()):
@@ -280,9 +273,8 @@ class PageSplitBackend:
         if B and not capturing and int((nv_g // N).min()) < self.sink_pages + self.local_pages:
             raise ValueError("every rank needs at least sink_pages + local_pages pages "
                              "of every sequence")
-        tau = torch.tensor(self.tau, dtype=torch.float32)
         scores = self.ops.score_pages(q, k, bt, cl, H, G, bs)          # [B, H, W_r] f32
-        s_all = torch.logsumexp(scores, -1)                     # [B, H], every valid page
+        BH = B * H
         reuse = None            # device bool: the cached selection passed the lazy gate
         if check:
             # lazy accounting of backend.py:420-465: every check counts; a layer
@@ -291,9 +283,10 @@ class PageSplitBackend:
         if check and cached is None:
             self._host["reject_steps"] += 1
         if check and cached is not None:
-            got = yield _pack(s_all, lse_sel(scores, *cached))
-            pa, ps = _unpack(got, (B, H), (B, H))
-            acc0 = coverage(pa, ps) >= tau
+            # each rank's log-sum-exps over its pages (all, cached selection);
+            # the gate takes them over the ranks
+            got = yield _pack(*self.ops.page_lse(scores, *cached))
+            acc0 = self.ops.rank_accept(got, 0, BH, BH, self.tau).view(B, H)
             self._host["heads_total"] += acc0.numel()
             reuse = acc0.all()
             ctr[self._C_HEADS_ACC] += acc0.sum()
@@ -337,8 +330,8 @@ class PageSplitBackend:
             idx_new = torch.where(reuse, cached[0], idx_new)
             n_new = torch.where(reuse, cached[1], n_new)
         idx_new, n_new = idx_new.contiguous(), n_new.contiguous()
-        got, (pa, ps) = yield from exchange_partial(idx_new, n_new,
-                                                    (s_all, lse_sel(scores, idx_new, n_new)))
+        got, _ = yield from exchange_partial(idx_new, n_new,
+                                             self.ops.page_lse(scores, idx_new, n_new))
         self.ops.rank_merge(got, B, H, G, D, out)
         if cached is not None and cached[0].shape == idx_new.shape:
             # in place: a captured reuse step keeps reading the same buffers
@@ -346,7 +339,7 @@ class PageSplitBackend:
             cached[1].copy_(n_new)
         else:
             self._cached[layer_idx] = (idx_new, n_new)
-        acc = coverage(pa, ps) >= tau
+        acc = self.ops.rank_accept(got, n_part, n_part + BH, BH, self.tau).view(B, H)
         if not self.lazy:
             ctr[self._C_HEADS_ACC] += acc.sum()
             self._host["heads_total"] += acc.numel()

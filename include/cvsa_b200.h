@@ -190,6 +190,25 @@ int cvsa_rank_merge(const float* parts, int32_t world, int64_t row_stride, int32
                     int32_t num_kv_heads, int32_t num_q_per_kv, int32_t head_dim,
                     const uint8_t* need, void* out, int32_t out_dtype, void* stream);
 
+/* The two log-sum-exps of the coverage gate per (sequence, KV head) row of
+ * page scores [rows, max_pages] f32: lse_all over every entry (-inf entries
+ * carry no mass) and lse_sel over the first n_per_head entries of the row's
+ * page_indices [rows, max_sel] (indices outside [0, max_pages) skipped);
+ * -inf when empty. A page-split rank exchanges these instead of its scores:
+ * coverage = exp(lse_sel - lse_all) of cvsa/kernels/coverage.py:179-215,
+ * with the sums taken over the ranks (cvsa_rank_accept). */
+int cvsa_page_lse(const float* page_scores, int32_t rows, int32_t max_pages,
+                  const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
+                  float* lse_all, float* lse_sel, void* stream);
+
+/* The coverage gate of a page split: for each of `rows` rows, coverage =
+ * exp(LSE_r sel_r - LSE_r all_r) over the `world` gathered rows of parts
+ * (rank r's lse_all at parts[r * row_stride + off_all + i], lse_sel at
+ * off_sel + i), accept[i] = coverage >= tau (uint8), the decision of
+ * cvsa/kernels/coverage.py:205-215. */
+int cvsa_rank_accept(const float* parts, int32_t world, int64_t row_stride, int64_t off_all,
+                     int64_t off_sel, int32_t rows, float tau, uint8_t* accept, void* stream);
+
 /* Fused exact recovery: for heads with accept == 0, attend to the valid pages
  * NOT in the selection (skipped through a selection bitmap, never
  * materialised as an index list) and LSE-merge that complement partial with

@@ -83,6 +83,10 @@ def test_validation_rejects_before_any_cuda_call():
     assert b"row_stride" in lib.cvsa_last_error()
     assert lib.cvsa_rank_merge(16, 2, 2 * 32 * 130, 2, 8, 4, 128, None, 16, 9, None) \
         == _lib.ERR_INVALID
+    # page-split coverage sums and gate: empty widths, offsets past the row
+    assert lib.cvsa_page_lse(16, 8, 0, 16, 4, 16, 16, 16, None) == _lib.ERR_INVALID
+    assert lib.cvsa_rank_accept(16, 2, 100, 0, 90, 16, 0.9, 16, None) == _lib.ERR_INVALID
+    assert lib.cvsa_rank_accept(16, 0, 100, 0, 16, 16, 0.9, 16, None) == _lib.ERR_INVALID
 
 
 def test_status_codes_map_to_reference_exceptions():

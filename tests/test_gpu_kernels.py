@@ -299,3 +299,37 @@ def test_rank_merge_vs_fp32_formula(cuda, world):
     nq = need.repeat_interleave(G, dim=1).unsqueeze(-1)
     want = torch.where(nq, ref, keep)
     assert (got.cpu() - want).abs().max() < 1e-5
+
+
+def test_page_lse_and_rank_accept_vs_fp32(cuda):
+    """cvsa_page_lse against torch.logsumexp (pages past the context at -inf,
+    a row with no valid page, a head with an empty selection), then
+    cvsa_rank_accept against the fp32 gate over 3 ranks' gathered sums."""
+    from cvsa.kernels.coverage import page_lse, rank_accept
+    g = torch.Generator().manual_seed(5)
+    B, H, W, K = 3, 8, 700, 40
+    scores = torch.randn(B, H, W, generator=g) * 4
+    scores[:, :, 650:] = float("-inf")
+    scores[0, 0] = float("-inf")
+    idx = torch.sort(torch.randint(0, 650, (B, H, K), generator=g), -1).values.to(torch.int32)
+    n = torch.randint(0, K + 1, (B, H), generator=g).to(torch.int32)
+    n[1, 1] = 0
+    mask = torch.arange(K).view(1, 1, K) < n.unsqueeze(-1)
+    sel = torch.gather(scores, -1, idx.long()).masked_fill(~mask, float("-inf"))
+    ref_all, ref_sel = torch.logsumexp(scores, -1), torch.logsumexp(sel, -1)
+    la, ls = page_lse(scores.to(cuda), idx.to(cuda), n.to(cuda))
+    for got, ref in ((la.cpu(), ref_all), (ls.cpu(), ref_sel)):
+        assert torch.equal(torch.isinf(got), torch.isinf(ref))
+        fin = torch.isfinite(ref)
+        assert ((got[fin] - ref[fin]).abs() <= 1e-5 + 1e-6 * ref[fin].abs()).all()
+    world, R = 3, B * H
+    sa = torch.randn(world, R, generator=g) + 5
+    ss = sa - torch.rand(world, R, generator=g) * 0.4
+    ss[1, :4] = float("-inf")                               # a rank with no selected page
+    parts = torch.cat([torch.randn(world, 5, generator=g), sa, ss,
+                       torch.randn(world, 3, generator=g)], 1).contiguous()
+    cov = torch.exp(torch.logsumexp(ss, 0) - torch.logsumexp(sa, 0))
+    tau = float(cov.median())
+    acc = rank_accept(parts.to(cuda), 5, 5 + R, R, tau).cpu()
+    clear = (cov - tau).abs() > 1e-5
+    assert torch.equal(acc[clear], (cov >= tau)[clear])

@@ -46,6 +46,22 @@ class OracleOps:
         return out
 
     @staticmethod
+    def page_lse(scores, idx, n):
+        """log-sum-exp over every page and over the first n selected pages
+        (the two sums of coverage.py:179-215)."""
+        K = idx.shape[-1]
+        mask = torch.arange(K).view(1, 1, K) < n.unsqueeze(-1)
+        sel = torch.gather(scores, -1, idx.long().clamp(min=0)).masked_fill(~mask,
+                                                                             float("-inf"))
+        return torch.logsumexp(scores, -1), torch.logsumexp(sel, -1)
+
+    @staticmethod
+    def rank_accept(parts, off_all, off_sel, rows, tau):
+        lse_all = torch.logsumexp(parts[:, off_all:off_all + rows], 0)
+        lse_sel = torch.logsumexp(parts[:, off_sel:off_sel + rows], 0)
+        return torch.exp(lse_sel - lse_all) >= tau
+
+    @staticmethod
     def rank_merge(parts, B, H, G, D, out, need=None):
         """The LSE merge of cvsa/lse_merge.py:11-54 taken over the ranks
         (dim 0), in rank order, normalised by max(l, 1e-6)."""
