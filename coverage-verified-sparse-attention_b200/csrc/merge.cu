@@ -87,8 +87,11 @@ __global__ void rank_merge_kernel(const float* __restrict__ parts, int world, in
 
 // Per (sequence, KV head) row of page scores: log-sum-exp over the W entries
 // (-inf entries carry no mass) and over the first n entries of the row's
-// selection (entries outside [0, W) are skipped); -inf when empty. One warp
-// per row, an online (max, sum) per lane combined across the warp.
+// selection (entries outside [0, W) are skipped); -inf when empty. One CTA
+// of kLseThreads per row (a row can hold thousands of pages): an online
+// (max, sum) per thread, combined across each warp and then across warps.
+constexpr int kLseThreads = 256;
+
 __device__ __forceinline__ void lse_push(float& m, float& s, float x) {
   if (x == neg_inf()) return;
   if (x > m) {
@@ -99,7 +102,9 @@ __device__ __forceinline__ void lse_push(float& m, float& s, float x) {
   }
 }
 
-__device__ __forceinline__ float lse_warp(float m, float s) {
+// (m, s) pairs of the warp's lanes combined in place (every lane ends with
+// the warp's pair).
+__device__ __forceinline__ void lse_warp_pair(float& m, float& s) {
   for (int o = 16; o > 0; o >>= 1) {
     const float mo = __shfl_xor_sync(0xffffffffu, m, o);
     const float so = __shfl_xor_sync(0xffffffffu, s, o);
@@ -108,31 +113,48 @@ __device__ __forceinline__ float lse_warp(float m, float s) {
     s = (m == neg_inf() ? 0.f : s * expf(m - M)) + (mo == neg_inf() ? 0.f : so * expf(mo - M));
     m = M;
   }
+}
+
+__device__ __forceinline__ float lse_value(float m, float s) {
   return m == neg_inf() ? neg_inf() : m + logf(s);
 }
 
-__global__ void page_lse_kernel(const float* __restrict__ scores, int rows, int W,
-                                const int32_t* __restrict__ idx, int max_sel,
-                                const int32_t* __restrict__ n, float* __restrict__ lse_all,
-                                float* __restrict__ lse_sel) {
-  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+__global__ void __launch_bounds__(kLseThreads)
+page_lse_kernel(const float* __restrict__ scores, int W, const int32_t* __restrict__ idx,
+                int max_sel, const int32_t* __restrict__ n, float* __restrict__ lse_all,
+                float* __restrict__ lse_sel) {
+  constexpr int kWarps = kLseThreads / 32;
+  __shared__ float part_m[2][kWarps], part_s[2][kWarps];
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const float* sr = scores + (int64_t)row * W;
-  float m = neg_inf(), s = 0.f;
-  for (int p = lane; p < W; p += 32) lse_push(m, s, sr[p]);
-  const float all = lse_warp(m, s);
-  m = neg_inf();
-  s = 0.f;
+  float ma = neg_inf(), sa = 0.f, msel = neg_inf(), ssel = 0.f;
+  for (int p = threadIdx.x; p < W; p += kLseThreads) lse_push(ma, sa, sr[p]);
   const int cnt = min(n[row], max_sel);
-  for (int j = lane; j < cnt; j += 32) {
+  for (int j = threadIdx.x; j < cnt; j += kLseThreads) {
     const int p = idx[(int64_t)row * max_sel + j];
-    if (p >= 0 && p < W) lse_push(m, s, sr[p]);
+    if (p >= 0 && p < W) lse_push(msel, ssel, sr[p]);
   }
-  const float sel = lse_warp(m, s);
+  lse_warp_pair(ma, sa);
+  lse_warp_pair(msel, ssel);
   if (lane == 0) {
-    lse_all[row] = all;
-    lse_sel[row] = sel;
+    part_m[0][warp] = ma;
+    part_s[0][warp] = sa;
+    part_m[1][warp] = msel;
+    part_s[1][warp] = ssel;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    ma = lane < kWarps ? part_m[0][lane] : neg_inf();
+    sa = lane < kWarps ? part_s[0][lane] : 0.f;
+    msel = lane < kWarps ? part_m[1][lane] : neg_inf();
+    ssel = lane < kWarps ? part_s[1][lane] : 0.f;
+    lse_warp_pair(ma, sa);
+    lse_warp_pair(msel, ssel);
+    if (lane == 0) {
+      lse_all[row] = lse_value(ma, sa);
+      lse_sel[row] = lse_value(msel, ssel);
+    }
   }
 }
 
@@ -150,9 +172,7 @@ __global__ void rank_accept_kernel(const float* __restrict__ parts, int world, i
     lse_push(ma, sa, parts[r * stride + off_all + i]);
     lse_push(ms, ss, parts[r * stride + off_sel + i]);
   }
-  const float la = ma == neg_inf() ? neg_inf() : ma + logf(sa);
-  const float ls = ms == neg_inf() ? neg_inf() : ms + logf(ss);
-  accept[i] = expf(ls - la) >= tau ? 1 : 0;
+  accept[i] = expf(lse_value(ms, ss) - lse_value(ma, sa)) >= tau ? 1 : 0;
 }
 
 }  // namespace
@@ -216,9 +236,7 @@ cudaError_t launch_page_lse(const float* scores, int rows, int W, const int32_t*
                             int max_sel, const int32_t* n, float* lse_all, float* lse_sel,
                             cudaStream_t s) {
   if (rows == 0) return cudaSuccess;
-  const int wpb = 8;
-  page_lse_kernel<<<(rows + wpb - 1) / wpb, wpb * 32, 0, s>>>(scores, rows, W, idx, max_sel, n,
-                                                              lse_all, lse_sel);
+  page_lse_kernel<<<rows, kLseThreads, 0, s>>>(scores, W, idx, max_sel, n, lse_all, lse_sel);
   return cudaGetLastError();
 }
 
