@@ -721,11 +721,45 @@ static __device__ __align__(256) uint8_t g_noalloc_scratch[CVSA_NOALLOC_SCRATCH_
 
 namespace {
 
-// Device address of g_noalloc_scratch, looked up once per device (the name is
-// only a host-side stand-in for the symbol, not a device pointer).
+// Identity of the calling thread's current CUDA context (the driver's context
+// id, unique for the life of the process), or 0 if it cannot be read. The
+// driver functions are looked up through the runtime, so the library needs no
+// link against libcuda.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(f);
+    f = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(f);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
+// Device address of g_noalloc_scratch in the current context (the name is
+// only a host-side stand-in for the symbol, not a device pointer). It is
+// looked up once per device and context: after cudaDeviceReset, or when the
+// primary context is destroyed and created again, the module is loaded anew
+// and the array may sit at another address, so a new context id means a new
+// lookup. Without a readable context id the lookup runs on every call.
 void* noalloc_scratch_ptr(int* status) {
   static std::mutex mu;
   static void* ptrs[64] = {};
+  static unsigned long long ctx_ids[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) {
@@ -736,8 +770,11 @@ void* noalloc_scratch_ptr(int* status) {
     *status = fail(CVSA_ERR_UNSUPPORTED, "device ordinal %d above 63", dev);
     return nullptr;
   }
+  // (0 before the runtime has made a context current on this thread: the
+  // lookup below does, and the next call caches under the real id)
+  const unsigned long long id = current_context_id();
   std::lock_guard<std::mutex> lock(mu);
-  if (!ptrs[dev]) {
+  if (!ptrs[dev] || id == 0 || ctx_ids[dev] != id) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p) {
@@ -746,6 +783,7 @@ void* noalloc_scratch_ptr(int* status) {
       return nullptr;
     }
     ptrs[dev] = p;
+    ctx_ids[dev] = id;
   }
   *status = CVSA_OK;
   return ptrs[dev];

@@ -1,6 +1,6 @@
 // Shared device helpers for the CVSA sm_100a kernels: element conversion,
 // warp reductions, order-preserving float keys, and thin inline-PTX wrappers
-// for mbarriers, TMA tensor loads, ldmatrix and mma.sync.
+// for mbarriers, bulk copies, ldmatrix and mma.sync.
 #pragma once
 
 #include <cuda.h>
@@ -123,7 +123,7 @@ __device__ __forceinline__ float softmax_exp(float x) {
 }
 
 // ---------------------------------------------------------------------------
-// mbarrier / TMA / proxy fences (sm_90+ PTX, used on sm_100a)
+// mbarrier / bulk copies / proxy fences (sm_90+ PTX, used on sm_100a)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -175,29 +175,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// 3-D tiled TMA load (this CTA only) into this CTA's shared memory, completing
-// on `bar` with complete_tx. Coordinates are element indices (x innermost).
-__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map,
-                                            uint64_t* bar, int x, int y, int z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];"
-      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
-        "r"(x), "r"(y), "r"(z)
-      : "memory");
-}
-
-// 4-D tiled TMA load (this CTA only); coordinates innermost first.
-__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map,
-                                            uint64_t* bar, int x, int y, int z, int w) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2];"
-      ::"r"(smem_u32(smem_dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)),
-        "r"(x), "r"(y), "r"(z), "r"(w)
-      : "memory");
-}
-
 // 16-byte asynchronous global -> shared copy that bypasses L1 (streamed
 // data), with an L2 cache policy (`policy` from make_evict_first_policy).
 __device__ __forceinline__ void cp_async16(uint32_t smem_dst, const void* src, uint64_t policy) {
@@ -239,10 +216,6 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
       " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
       "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
 // ---------------------------------------------------------------------------

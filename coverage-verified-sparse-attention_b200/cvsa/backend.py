@@ -187,8 +187,12 @@ class CVSABackend:
         self._track_timing = False
         self._timing_events = None   # caller-owned cudaEvent_t array (bench.py)
         self._pending_events: list = []
+        # the reference's buckets (backend.py:217-220) plus 'dense'; the
+        # complement and the LSE merge run inside the attention kernel, so
+        # their buckets stay at zero and the time counts under 'ar_recovery'
         self._kernel_times_ms = {"scoring": 0.0, "coverage": 0.0, "sparse_draft": 0.0,
-                                 "ar_recovery": 0.0, "dense": 0.0}
+                                 "ar_recovery": 0.0, "lse_merge": 0.0, "complement": 0.0,
+                                 "dense": 0.0}
         self._kernel_counts = {k: 0 for k in self._kernel_times_ms}
 
     # ---- bookkeeping (backend.py:225-311) -------------------------------
@@ -196,8 +200,10 @@ class CVSABackend:
         """Per-kernel CUDA-event timing (backend.py:225-250). Buckets: 'scoring'
         (page scoring), 'coverage' (top-k selection + coverage gate),
         'sparse_draft' (attention of reuse steps), 'ar_recovery' (attention of
-        scoring steps: draft + complement recovery + merge, one kernel) and
-        'dense'. Recording events between kernels disables launch overlap."""
+        scoring steps: draft + complement recovery + merge, one kernel),
+        'lse_merge' and 'complement' (the reference's keys; always zero, as
+        that work is fused into 'ar_recovery') and 'dense'. Recording events
+        between kernels disables launch overlap."""
         self._track_timing = track
 
     def _flush_timing(self):

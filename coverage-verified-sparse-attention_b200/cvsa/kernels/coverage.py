@@ -114,12 +114,20 @@ def page_lse(page_scores: torch.Tensor, page_indices: torch.Tensor, n_per_head: 
     ps = page_scores.float().contiguous()
     pi = page_indices.to(torch.int32).reshape(B, H, -1).contiguous()
     nph = n_per_head.to(torch.int32).reshape(B, H).contiguous()
+    if W == 0:
+        # no page: both log-sum-exps are over an empty set (no launch)
+        lse_all = torch.full((B, H), float("-inf"), dtype=torch.float32, device=dev)
+        return lse_all, lse_all.clone()
+    if pi.shape[2] == 0:
+        # no selection slot: every row's selection is empty
+        pi = torch.zeros((B, H, 1), dtype=torch.int32, device=dev)
+        nph = torch.zeros((B, H), dtype=torch.int32, device=dev)
     lse_all = torch.empty((B, H), dtype=torch.float32, device=dev)
     lse_sel = torch.empty((B, H), dtype=torch.float32, device=dev)
     lib = _lib.load()
-    _lib.check(lib.cvsa_page_lse(ps.data_ptr(), B * H, max(W, 1), pi.data_ptr(),
-                                 max(pi.shape[2], 1), nph.data_ptr(), lse_all.data_ptr(),
-                                 lse_sel.data_ptr(), _lib.stream_ptr(dev)), "cvsa_page_lse")
+    _lib.check(lib.cvsa_page_lse(ps.data_ptr(), B * H, W, pi.data_ptr(), pi.shape[2],
+                                 nph.data_ptr(), lse_all.data_ptr(), lse_sel.data_ptr(),
+                                 _lib.stream_ptr(dev)), "cvsa_page_lse")
     return lse_all, lse_sel
 
 

@@ -158,8 +158,9 @@ class PageSplitBackend:
     global block-table width (the budget is int(W * budget_pct), backend.py:690).
     """
 
-    # device-side counters (the decisions never reach the host during a step)
-    _C_SCORING, _C_ACCEPT, _C_REJECT, _C_HEADS_ACC = range(4)
+    # device-side counters: the decisions never reach the host during a step,
+    # and a step captured in a CUDA graph counts on every replay
+    _C_SCORING, _C_ACCEPT, _C_REJECT, _C_HEADS_ACC, _C_CHECKS, _C_HEADS_TOTAL = range(6)
 
     def __init__(self, num_kv_heads: int, num_q_heads: int, head_dim: int, block_size: int,
                  rank: int, world: int, num_layers: int = 32, budget_pct: float = 0.10,
@@ -183,20 +184,16 @@ class PageSplitBackend:
         self.ops = ops or DeviceOps()
         self._cached: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
         self._step = 0
-        self._host = dict(scoring_steps=0, coverage_checks=0, reject_steps=0, heads_total=0)
         self._ctr: Optional[torch.Tensor] = None
 
     @property
     def stats(self) -> Dict[str, int]:
         """scoring_steps, coverage_checks, accept_steps, reject_steps,
         heads_accepted, heads_total (reads the device counters)."""
-        c = self._ctr.tolist() if self._ctr is not None else [0, 0, 0, 0]
-        h = self._host
-        return dict(scoring_steps=h["scoring_steps"] + c[self._C_SCORING],
-                    coverage_checks=h["coverage_checks"],
-                    accept_steps=c[self._C_ACCEPT],
-                    reject_steps=h["reject_steps"] + c[self._C_REJECT],
-                    heads_accepted=c[self._C_HEADS_ACC], heads_total=h["heads_total"])
+        c = self._ctr.tolist() if self._ctr is not None else [0] * 6
+        return dict(scoring_steps=c[self._C_SCORING], coverage_checks=c[self._C_CHECKS],
+                    accept_steps=c[self._C_ACCEPT], reject_steps=c[self._C_REJECT],
+                    heads_accepted=c[self._C_HEADS_ACC], heads_total=c[self._C_HEADS_TOTAL])
 
     def step_done(self, layer_idx: int, num_layers: int):
         if layer_idx == num_layers - 1:
@@ -214,7 +211,7 @@ class PageSplitBackend:
 
     def _counters(self, dev) -> torch.Tensor:
         if self._ctr is None:
-            self._ctr = torch.zeros(4, dtype=torch.int64, device=dev)
+            self._ctr = torch.zeros(6, dtype=torch.int64, device=dev)
         return self._ctr
 
     # ---- the step ---------------------------------------------------------
@@ -279,22 +276,22 @@ class PageSplitBackend:
         if check:
             # lazy accounting of backend.py:420-465: every check counts; a layer
             # without a cached selection counts as a reject
-            self._host["coverage_checks"] += 1
+            ctr[self._C_CHECKS] += 1
         if check and cached is None:
-            self._host["reject_steps"] += 1
+            ctr[self._C_REJECT] += 1
         if check and cached is not None:
             # each rank's log-sum-exps over its pages (all, cached selection);
             # the gate takes them over the ranks
             got = yield _pack(*self.ops.page_lse(scores, *cached))
             acc0 = self.ops.rank_accept(got, 0, BH, BH, self.tau).view(B, H)
-            self._host["heads_total"] += acc0.numel()
+            ctr[self._C_HEADS_TOTAL] += acc0.numel()
             reuse = acc0.all()
             ctr[self._C_HEADS_ACC] += acc0.sum()
             ctr[self._C_ACCEPT] += reuse
             ctr[self._C_REJECT] += ~reuse
             ctr[self._C_SCORING] += ~reuse
         else:
-            self._host["scoring_steps"] += 1
+            ctr[self._C_SCORING] += 1
 
         # ---- scoring step (gated by `reuse` on a lazy check step) ----
         # proposals: this rank's selection at the common width max_sel, page
@@ -342,7 +339,7 @@ class PageSplitBackend:
         acc = self.ops.rank_accept(got, n_part, n_part + BH, BH, self.tau).view(B, H)
         if not self.lazy:
             ctr[self._C_HEADS_ACC] += acc.sum()
-            self._host["heads_total"] += acc.numel()
+            ctr[self._C_HEADS_TOTAL] += acc.numel()
         # exact recovery: rejected heads attend every valid page of the range
         # and their merged result replaces the draft; heads that need none
         # (accepted, or the cached selection passed the lazy gate) attend no

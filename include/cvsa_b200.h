@@ -371,7 +371,10 @@ int cvsa_paged_gather(const cvsa_kv_desc_t* kv, const int32_t* block_table_row,
  * counterpart in the reference.
  *   - The first call on a device looks up that array's device address with
  *     cudaGetSymbolAddress (the current device must be the one decoding);
- *     make that first call before any stream capture.
+ *     make that first call before any stream capture. The address is kept
+ *     per device and CUDA context: after cudaDeviceReset (or any other end of
+ *     the context) the next call looks it up again, so that call too must
+ *     come before a capture.
  *   - Shapes whose scratch would exceed CVSA_NOALLOC_SCRATCH_BYTES are
  *     rejected with CVSA_ERR_UNSUPPORTED and a message naming both sizes.
  *   - Every call on a device shares the one array, and each call clears the
