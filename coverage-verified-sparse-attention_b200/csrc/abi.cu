@@ -204,6 +204,25 @@ int cvsa_score_pages(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd, flo
                      "score_pages launch");
 }
 
+int cvsa_quest_scores(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd, float* page_scores,
+                      int32_t* dev_error, void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (!page_scores) return fail(CVSA_ERR_INVALID, "page_scores is NULL");
+  if (!quest_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED,
+                "quest scoring built for block_size 16, head_dim 64/128/256 (fp32: 64/128), "
+                "num_kv_heads * head_dim <= 12288");
+  if (q.B == 0) return CVSA_OK;
+  return cuda_status(launch_quest_scores(q, kv, page_scores, dev_error, (cudaStream_t)stream,
+                                         false),
+                     "quest_scores launch");
+}
+
 int cvsa_select_pages(const float* page_scores, int32_t batch, int32_t num_kv_heads,
                       int32_t max_pages, const int32_t* context_lens, int32_t block_size,
                       int32_t budget, int32_t sink_pages, int32_t local_pages,

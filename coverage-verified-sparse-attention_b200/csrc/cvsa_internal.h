@@ -52,6 +52,11 @@ cudaError_t launch_score_pages(const QView& q, const KvView& kv, float* scores,
                                int32_t* dev_err, cudaStream_t s, bool pdl);
 bool score_supported(const QView& q, const KvView& kv);
 
+// ---- quest.cu ----
+cudaError_t launch_quest_scores(const QView& q, const KvView& kv, float* scores,
+                                int32_t* dev_err, cudaStream_t s, bool pdl);
+bool quest_supported(const QView& q, const KvView& kv);
+
 // ---- select.cu ----
 struct SelectParams {
   const float* scores;        // [B, Hkv, W]

@@ -85,6 +85,8 @@ _SIGS = {
     "cvsa_status_string": ([ctypes.c_int], ctypes.c_char_p),
     "cvsa_last_error": ([], ctypes.c_char_p),
     "cvsa_score_pages": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _P], ctypes.c_int),
+    "cvsa_quest_scores": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _P, _P],
+                          ctypes.c_int),
     "cvsa_select_pages": ([_P, _I, _I, _I, _P, _I, _I, _I, _I, _P, _I, _P, _P], ctypes.c_int),
     "cvsa_check_coverage": ([_P, _I, _I, _I, _P, _I, _P, ctypes.c_float, _P, _P, _P], ctypes.c_int),
     "cvsa_compute_complement": ([_P, _I, _P, _P, _I, _I, _I, _P, _P, _I, _P, _P], ctypes.c_int),

@@ -28,11 +28,12 @@ process per GPU; this rank holds `num_kv_heads` of them with their
 `num_q_heads` query heads), and the lazy step's batch-global decision is
 all-reduced (MIN of one int32) over the group between the selection and the
 attention kernels, so every rank reuses or re-selects together exactly as
-one GPU holding all heads would. Options of the
-reference that select pages differently (adaptive_selection,
-static_budget_table, selector='quest', top_p, light_normalizer) and the
-random-reject counterfactual are not implemented by this backend yet and
-raise NotImplementedError when requested. A coverage_interval below
+one GPU holding all heads would. The reference's options that select
+pages differently (selector='quest' and light_normalizer, top_p,
+static_budget_table, adaptive_selection) and the random-reject
+counterfactual (random_reject_prob) run as host-orchestrated steps over the
+same kernels plus the Quest sketch kernel (cvsa/selectors.py), reading the
+decisions on the host where the reference does. A coverage_interval below
 check_interval runs the reference's coverage-only steps (backend.py:467-520):
 the cached selection is gated on the page scores kept from the last scoring
 step, and the host reads the decision, as the reference does. Approximate recovery (approx_recovery_pct, backend.py:780-817)
@@ -132,22 +133,16 @@ class CVSABackend:
             raise ValueError("num_q_heads must be a multiple of num_kv_heads")
         if sink_pages < 0 or local_pages < 0:
             raise ValueError("sink_pages/local_pages must be >= 0")
-        unsupported = []
         if approx_recovery_pct is not None and not (0.0 < approx_recovery_pct <= 1.0):
             raise ValueError(f"approx_recovery_pct must be in (0, 1], got {approx_recovery_pct}")
-        if adaptive_selection:
-            unsupported.append("adaptive_selection")
-        if random_reject_prob is not None:
-            unsupported.append("random_reject_prob")
-        if static_budget_table is not None:
-            unsupported.append("static_budget_table")
-        if selector != "exact":
-            unsupported.append("selector='quest'")
-        if top_p is not None:
-            unsupported.append("top_p")
-        if unsupported:
-            raise NotImplementedError("not implemented by the B200 backend: " +
-                                      ", ".join(unsupported))
+        alt = (selector != "exact" or light_normalizer or top_p is not None
+               or static_budget_table is not None or adaptive_selection
+               or random_reject_prob is not None)
+        if alt and (sink_pages or local_pages):
+            raise ValueError("sink_pages/local_pages apply to the uniform top-k only, "
+                             "not with the reference's selector options")
+        if alt and process_group is not None:
+            raise ValueError("the selector options run on one GPU (no process_group)")
 
         self.num_kv_heads = num_kv_heads
         self.num_q_heads = num_q_heads
@@ -194,6 +189,12 @@ class CVSABackend:
                                  "ar_recovery": 0.0, "lse_merge": 0.0, "complement": 0.0,
                                  "dense": 0.0}
         self._kernel_counts = {k: 0 for k in self._kernel_times_ms}
+        # the reference's selector options run as host-orchestrated steps over
+        # the same kernels (cvsa/selectors.py); None: the fused C-ABI step
+        self._alt = None
+        if alt:
+            from cvsa.selectors import AltStep
+            self._alt = AltStep(self)
 
     # ---- bookkeeping (backend.py:225-311) -------------------------------
     def enable_timing(self, track: bool = True):
@@ -228,6 +229,8 @@ class CVSABackend:
         self._step = 0
         for st in self._layers.values():
             st.has_cache = False
+        if self._alt is not None:
+            self._alt.reset()
         self._last_accept_mask = {}
         self._last_expanded_selection = {}
         if self._counters is not None:
@@ -346,6 +349,14 @@ class CVSABackend:
             q = q.squeeze(1)
         dev = _lib.require_cuda(q, k_cache, v_cache, block_tables, context_lens)
         self._ensure(dev)
+        if self._alt is not None and layer_idx not in self._dense_layers:
+            bt_a = block_tables if block_tables.dtype == torch.int32 else \
+                block_tables.to(torch.int32)
+            cl_a = context_lens if context_lens.dtype == torch.int32 else \
+                context_lens.to(torch.int32)
+            out = self._alt(q.contiguous(), k_cache, v_cache, bt_a.contiguous(),
+                            cl_a.contiguous(), layer_idx)
+            return StepHandle(out, None, None)
         B, Hq, D = q.shape
         W = block_tables.shape[1]
         budget = budget_for(W, self.budget_pct)
@@ -498,7 +509,10 @@ class CVSABackend:
 
     # ---- tracing helpers -------------------------------------------------
     def cached_selection(self, layer_idx: int) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
-        """(page_indices [B,H_kv,max_sel] ascending, n_per_head) cached for a layer."""
+        """(page_indices [B,H_kv,max_sel], n_per_head) cached for a layer: ascending
+        page order, or score order for the per-head-budget selectors."""
+        if self._alt is not None and layer_idx in self._alt.cached:
+            return self._alt.cached[layer_idx]
         st = self._layers.get(layer_idx)
         if st is None or not st.has_cache:
             return None

@@ -109,6 +109,17 @@ const char* cvsa_last_error(void);
 int cvsa_score_pages(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
                      float* page_scores, void* stream);
 
+/* Quest page ranking scores, [batch, num_kv_heads, max_pages] float32: per
+ * page and KV head, the channel-wise minimum and maximum of the keys of its
+ * valid tokens, then sum_d max(q_d * kmin_d, q_d * kmax_d) * head_dim^-0.5 with
+ * q the group mean of the query heads rounded to q's dtype; -inf for pages
+ * without a valid token. A block id outside the pool sets
+ * CVSA_DEV_ERR_BLOCK_RANGE in *dev_error (nullable) and scores -inf.
+ * Replaces CVSABackend._quest_page_scores, cvsa/backend.py:572-620 (the
+ * selector='quest' / light_normalizer ranking). */
+int cvsa_quest_scores(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                      float* page_scores, int32_t* dev_error, void* stream);
+
 /* Top-k page selection per (b, kv head): the first `sink_pages` and last
  * `local_pages` valid pages, plus the `budget` highest-scoring other valid
  * pages, ordered (score desc, page index asc); written in ascending page

@@ -416,6 +416,178 @@ def scoring_step(q, k_cache, v_cache, block_tables, context_lens, num_kv_heads,
                 budget=torch.tensor(budget))
 
 
+# --------------------------------------------------------------------------
+# alternative selectors (cvsa/backend.py:522-681)
+# --------------------------------------------------------------------------
+
+def quest_page_scores(q: torch.Tensor, k_cache: torch.Tensor, block_tables: torch.Tensor,
+                      context_lens: torch.Tensor, num_kv_heads: int,
+                      block_size: int) -> torch.Tensor:
+    """Quest ranking scores [B, H_kv, W] f32 (cvsa/backend.py:572-620).
+
+    For each page and KV head: the channel-wise minimum and maximum of the
+    keys of its valid tokens (in the pool's dtype), then
+    sum_d max(q_d * kmin_d, q_d * kmax_d) in fp32 with q the group mean in
+    q's dtype (as page scoring pools it), times D^-0.5. Pages without a valid
+    token score -inf.
+    """
+    B, W = block_tables.shape
+    D = q.shape[-1]
+    qr = q_representative(q, num_kv_heads).float()                # [B, H, D]
+    out = torch.full((B, num_kv_heads, W), NEG_INF, dtype=torch.float32)
+    for b in range(B):
+        ctx = int(context_lens[b])
+        n = min((ctx + block_size - 1) // block_size, W)
+        if n == 0:
+            continue
+        kp = k_cache[block_tables[b, :n].long()]                  # [n, bs, H, D]
+        tok = torch.arange(n).view(n, 1) * block_size + torch.arange(block_size).view(1, -1)
+        valid = (tok < ctx).view(n, block_size, 1, 1)
+        kmin = torch.where(valid, kp, torch.full_like(kp, math.inf)).amin(dim=1).float()
+        kmax = torch.where(valid, kp, torch.full_like(kp, -math.inf)).amax(dim=1).float()
+        qb = qr[b].view(1, num_kv_heads, D)
+        bound = torch.maximum(qb * kmin, qb * kmax).sum(-1) * (D ** -0.5)   # [n, H]
+        out[b, :, :n] = bound.t()
+    return out
+
+
+def _stable_desc_order(x: torch.Tensor) -> torch.Tensor:
+    """Indices ordering the last dim by (value descending, index ascending)."""
+    return torch.sort(x, dim=-1, descending=True, stable=True).indices
+
+
+def topp_select(sel_scores: torch.Tensor, n_valid: torch.Tensor, top_p: float):
+    """cvsa/backend.py:652-681: per head the shortest score-ordered prefix whose
+    softmax mass (over every page of the row) reaches top_p, at least 3 pages,
+    at most the valid ones. Returns (page_indices [B, H, max_budget] in score
+    order, n_per_head, max_budget)."""
+    B, H, P = sel_scores.shape
+    probs = torch.softmax(sel_scores.float(), dim=-1)
+    order = _stable_desc_order(probs)
+    mass = torch.gather(probs, -1, order).cumsum(-1)
+    need = ((mass < top_p).sum(-1) + 1).clamp(min=3, max=P)
+    n = torch.minimum(need, n_valid.view(B, 1).expand(B, H).to(need.dtype)).to(torch.int32)
+    mb = int(n.max())
+    return order[:, :, :mb].to(torch.int32), n, mb
+
+
+def static_select(sel_scores: torch.Tensor, fracs, n_valid: torch.Tensor):
+    """cvsa/backend.py:622-650: per-head budgets round(frac * W), clamped to
+    [3, W], at most the valid pages; the top pages of each head in score
+    order. Returns (page_indices, n_per_head, max_budget)."""
+    B, H, P = sel_scores.shape
+    f = torch.as_tensor(fracs, dtype=torch.float32)
+    per = torch.clamp((f * P).round().long(), min=3, max=P)
+    n = torch.minimum(per.view(1, H).expand(B, H), n_valid.view(B, 1).expand(B, H))
+    mb = int(per.max())
+    order = _stable_desc_order(sel_scores)[:, :, :min(mb, P)]
+    return order.to(torch.int32), n.to(torch.int32), mb
+
+
+def adaptive_select(page_scores: torch.Tensor, base_budget: int, n_valid: torch.Tensor,
+                    floor_ratio: float):
+    """cvsa/backend.py:522-570: the heads of a sequence compete for
+    H * base_budget page slots by score (each head's share = how many of the
+    H * base_budget best scores of the sequence are its), blended toward the
+    uniform budget by floor_ratio, rounded half to even, at least 1 and at most
+    the valid pages. Returns (page_indices in score order, n_per_head,
+    max_budget)."""
+    B, H, P = page_scores.shape
+    total = H * base_budget
+    flat = page_scores.reshape(B, H * P)
+    order = _stable_desc_order(flat)[:, :min(total, H * P)]
+    owner = order // P
+    wins = torch.zeros(B, H, dtype=torch.float32)
+    wins.scatter_add_(-1, owner, torch.ones_like(owner, dtype=torch.float32))
+    final = torch.round(wins * (1 - floor_ratio) + base_budget * floor_ratio).to(torch.int32)
+    final = torch.minimum(final.clamp(min=1), n_valid.view(B, 1).expand(B, H).to(torch.int32))
+    mb = int(final.max())
+    idx = _stable_desc_order(page_scores)[:, :, :min(mb, P)]
+    return idx.to(torch.int32), final, mb
+
+
+def uniform_select_unsorted_ref(sel_scores: torch.Tensor, n_valid: torch.Tensor, budget: int):
+    """The reference's uniform path (cvsa/backend.py:737-747) with the stable
+    tie rule: the top `budget` pages, n_per_head = min(budget, valid pages)."""
+    B, H, P = sel_scores.shape
+    idx = _stable_desc_order(sel_scores)[:, :, :min(budget, P)]
+    n = torch.minimum(torch.full((B, H), budget, dtype=torch.int64),
+                      n_valid.view(B, 1).expand(B, H)).to(torch.int32)
+    return idx.to(torch.int32), n, budget
+
+
+def alt_scoring_step(q, k_cache, v_cache, block_tables, context_lens, num_kv_heads,
+                     num_q_per_kv, block_size, budget_pct, tau, *, selector="exact",
+                     light_normalizer=False, top_p=None, static_fracs=None,
+                     adaptive=False, adaptive_floor_ratio=0.5, approx_recovery_pct=None,
+                     reject_override=None, page_scores=None, precise=True):
+    """cvsa/backend.py:683-864 with the reference's selector options.
+
+    `page_scores` drive the coverage gate (the Quest sketch when
+    light_normalizer, else exact); `sel_scores` drive the ranking (the sketch
+    when selector == 'quest'). reject_override: None, or True / False to force
+    every head to reject / accept (the random-reject counterfactual with its
+    draw already taken).
+    """
+    W = block_tables.shape[1]
+    nv = n_valid_pages(context_lens, block_size)
+    budget = budget_for(W, budget_pct)
+    quest = None
+    if page_scores is None:
+        if light_normalizer:
+            quest = quest_page_scores(q, k_cache, block_tables, context_lens, num_kv_heads,
+                                      block_size)
+            page_scores = quest
+        else:
+            page_scores = score_pages(q, k_cache, block_tables, context_lens, num_kv_heads,
+                                      num_q_per_kv, block_size, precise)
+    sel_scores = page_scores
+    if selector == "quest" and not light_normalizer:
+        quest = quest_page_scores(q, k_cache, block_tables, context_lens, num_kv_heads,
+                                  block_size)
+        sel_scores = quest
+    if top_p is not None:
+        idx, nph, budget = topp_select(sel_scores, nv, top_p)
+    elif static_fracs is not None:
+        idx, nph, budget = static_select(sel_scores, static_fracs, nv)
+    elif adaptive:
+        idx, nph, budget = adaptive_select(sel_scores, budget, nv, adaptive_floor_ratio)
+    else:
+        idx, nph, budget = uniform_select_unsorted_ref(sel_scores, nv, budget)
+    o_d, m_d, l_d = sparse_decode_unnorm(q, k_cache, v_cache, block_tables, idx, nph,
+                                         context_lens, num_kv_heads, num_q_per_kv,
+                                         block_size, precise)
+    accept, cov = check_coverage(page_scores, idx, nph, tau, precise)
+    if reject_override is not None:
+        accept = torch.full_like(accept, not reject_override)
+    exp = None
+    if bool(accept.all()):
+        out = (o_d / l_d.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
+        n_rec = torch.zeros_like(nph)
+    elif approx_recovery_pct is not None:
+        eb = min(max(budget + 1, int(W * approx_recovery_pct)), W)
+        e_idx = _stable_desc_order(sel_scores)[:, :, :eb].to(torch.int32)
+        e_n = torch.minimum(torch.full_like(nph, eb), nv.view(-1, 1).expand_as(nph).to(nph.dtype))
+        o_e, m_e, l_e = sparse_decode_unnorm(q, k_cache, v_cache, block_tables, e_idx, e_n,
+                                             context_lens, num_kv_heads, num_q_per_kv,
+                                             block_size, precise)
+        acc_q = accept.repeat_interleave(num_q_per_kv, dim=1).unsqueeze(-1)
+        out = torch.where(acc_q, o_d / l_d.clamp(min=1e-6).unsqueeze(-1),
+                          o_e / l_e.clamp(min=1e-6).unsqueeze(-1)).to(q.dtype)
+        n_rec = e_n
+        exp = (e_idx, e_n)
+    else:
+        comp, n_comp = compute_complement_pages(idx, nph, context_lens, block_size, accept)
+        o_c, m_c, l_c = sparse_decode_unnorm(q, k_cache, v_cache, block_tables, comp, n_comp,
+                                             context_lens, num_kv_heads, num_q_per_kv,
+                                             block_size, precise)
+        out = selective_lse_merge(o_d, m_d, l_d, o_c, m_c, l_c, accept, num_q_per_kv, q.dtype)
+        n_rec = n_comp
+    return dict(output=out, page_scores=page_scores, sel_scores=sel_scores, page_indices=idx,
+                n_per_head=nph, accept=accept, coverage=cov, n_recovery=n_rec, expanded=exp,
+                budget=budget)
+
+
 class OracleBackend:
     """Scheduling of cvsa/backend.py:313-366 / 392-465 / 866-881 on the oracle ops.
 
@@ -430,7 +602,9 @@ class OracleBackend:
                  budget_pct=0.10, reuse_interval=16, coverage_threshold=0.90,
                  dense_layers=None, lazy=False, check_interval=None,
                  sink_pages=0, local_pages=0, precise=True, approx_recovery_pct=None,
-                 coverage_interval=None):
+                 coverage_interval=None, selector="exact", light_normalizer=False,
+                 top_p=None, static_budget_table=None, adaptive_selection=False,
+                 adaptive_floor_ratio=0.5, random_reject_prob=None, reject_draw=None):
         self.num_kv_heads = num_kv_heads
         self.num_q_heads = num_q_heads
         self.G = num_q_heads // num_kv_heads
@@ -448,6 +622,19 @@ class OracleBackend:
         self.precise = precise
         self.approx_recovery_pct = approx_recovery_pct
         self.coverage_interval = coverage_interval or self.check_interval
+        # selector options of backend.py:66-76; reject_draw() gives the
+        # uniform [0, 1) draws of the random-reject counterfactual
+        self.selector = selector
+        self.light_normalizer = light_normalizer
+        self.top_p = top_p
+        self.static_budget_table = static_budget_table
+        self.adaptive_selection = adaptive_selection
+        self.adaptive_floor_ratio = adaptive_floor_ratio
+        self.random_reject_prob = random_reject_prob
+        self.reject_draw = reject_draw or (lambda: float(torch.rand(1)))
+        self.alt = (selector != "exact" or light_normalizer or top_p is not None
+                    or static_budget_table is not None or adaptive_selection
+                    or random_reject_prob is not None)
         self.reset()
 
     def reset(self):
@@ -480,10 +667,35 @@ class OracleBackend:
         return sparse_decode(q, k, v, bt, idx, nph, cl, self.num_kv_heads, self.G,
                              self.block_size, self.precise)
 
+    def _override(self):
+        """backend.py:437-438 / 764-766: one draw per gate, True = reject all."""
+        if self.random_reject_prob is None:
+            return None
+        return self.reject_draw() < self.random_reject_prob
+
+    def _gate_scores(self, q, k, bt, cl):
+        if self.light_normalizer:
+            return quest_page_scores(q, k, bt, cl, self.num_kv_heads, self.block_size)
+        return score_pages(q, k, bt, cl, self.num_kv_heads, self.G, self.block_size,
+                           self.precise)
+
     def _scoring(self, q, k, v, bt, cl, layer_idx, page_scores=None):
-        r = scoring_step(q, k, v, bt, cl, self.num_kv_heads, self.G, self.block_size,
-                         self.budget_pct, self.tau, self.sink_pages, self.local_pages,
-                         page_scores, self.precise, self.approx_recovery_pct)
+        if self.alt:
+            fr = None
+            if self.static_budget_table is not None:
+                fr = self.static_budget_table[layer_idx]
+            r = alt_scoring_step(q, k, v, bt, cl, self.num_kv_heads, self.G, self.block_size,
+                                 self.budget_pct, self.tau, selector=self.selector,
+                                 light_normalizer=self.light_normalizer, top_p=self.top_p,
+                                 static_fracs=fr, adaptive=self.adaptive_selection,
+                                 adaptive_floor_ratio=self.adaptive_floor_ratio,
+                                 approx_recovery_pct=self.approx_recovery_pct,
+                                 reject_override=self._override(), page_scores=page_scores,
+                                 precise=self.precise)
+        else:
+            r = scoring_step(q, k, v, bt, cl, self.num_kv_heads, self.G, self.block_size,
+                             self.budget_pct, self.tau, self.sink_pages, self.local_pages,
+                             page_scores, self.precise, self.approx_recovery_pct)
         self._cached[layer_idx] = (r["page_indices"], r["n_per_head"])
         self._cached_scores[layer_idx] = r["page_scores"]
         self._record(cl, r["n_per_head"].sum() + r["n_recovery"].sum())
@@ -524,6 +736,9 @@ class OracleBackend:
         idx, nph = self._cached[layer_idx]
         accept, cov = check_coverage(self._cached_scores[layer_idx], idx, nph, self.tau,
                                      self.precise)
+        ov = self._override()
+        if ov is not None:
+            accept = torch.full_like(accept, not ov)
         self.per_head_accept_sum += int(accept.sum())
         self.per_head_total += accept.numel()
         self.total_coverage_checks += 1
@@ -535,12 +750,14 @@ class OracleBackend:
         return self._scoring(q, k, v, bt, cl, layer_idx)
 
     def _lazy(self, q, k, v, bt, cl, layer_idx):
-        scores = score_pages(q, k, bt, cl, self.num_kv_heads, self.G, self.block_size,
-                             self.precise)
+        scores = self._gate_scores(q, k, bt, cl)
         self.total_coverage_checks += 1
         if layer_idx in self._cached:
             idx, nph = self._cached[layer_idx]
             accept, cov = check_coverage(scores, idx, nph, self.tau, self.precise)
+            ov = self._override()
+            if ov is not None:
+                accept = torch.full_like(accept, not ov)
             self.per_head_accept_sum += int(accept.sum())
             self.per_head_total += accept.numel()
             self.last = dict(cached_accept=accept, cached_coverage=cov, page_scores=scores)

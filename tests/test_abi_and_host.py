@@ -107,11 +107,18 @@ def test_backend_argument_checks_match_reference():
         CVSABackend(8, 32, 128, 16, light_normalizer=True)
     with pytest.raises(ValueError):
         CVSABackend(8, 32, 128, 16, top_p=1.5)
-    with pytest.raises(NotImplementedError):
-        CVSABackend(8, 32, 128, 16, adaptive_selection=True)
     with pytest.raises(ValueError):
         CVSABackend(8, 32, 128, 16, approx_recovery_pct=1.5)
     CVSABackend(8, 32, 128, 16, approx_recovery_pct=0.2)     # supported
+    # the reference's selector options construct (cvsa/selectors.py runs them)
+    for kw in (dict(adaptive_selection=True), dict(top_p=0.9), dict(selector="quest"),
+               dict(selector="quest", light_normalizer=True), dict(random_reject_prob=0.2),
+               dict(static_budget_table={0: [0.1] * 8})):
+        assert CVSABackend(8, 32, 128, 16, **kw)._alt is not None
+    assert CVSABackend(8, 32, 128, 16)._alt is None
+    # forced pages are an extension of the uniform top-k only
+    with pytest.raises(ValueError):
+        CVSABackend(8, 32, 128, 16, top_p=0.9, sink_pages=1)
 
 
 def test_budget_uses_table_width():
