@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -22,6 +23,9 @@ int dtype_bytes(int dtype) {
     default: return 0;
   }
 }
+
+std::atomic<uint32_t> g_wait_limit{0};
+uint32_t wait_limit() { return g_wait_limit.load(std::memory_order_relaxed); }
 
 int num_sms() {
   static int cache[64] = {};
@@ -187,6 +191,11 @@ const char* cvsa_status_string(int status) {
 }
 
 const char* cvsa_last_error(void) { return g_last_error.c_str(); }
+
+int cvsa_set_wait_limit(uint32_t polls) {
+  g_wait_limit.store(polls, std::memory_order_relaxed);
+  return CVSA_OK;
+}
 
 int cvsa_score_pages(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd, float* page_scores,
                      void* stream) {

@@ -122,6 +122,10 @@ struct StreamArgs {
   // the query rows of a CTA's first q_slots heads are copied into shared
   // memory at the start (one bulk copy per head on the mbarrier at off_qbar)
   int off_qbar, off_q, q_slots;
+  // polls of a bounded wait on another warp (the producer's descriptors, a
+  // free ring entry, the staged query rows) before it gives up; the waits
+  // that drain the CTA's own copies before it exits keep the default
+  uint32_t wait_polls;
   float scale;
 };
 
@@ -171,11 +175,12 @@ __device__ __forceinline__ int block_excl_scan(int v, int* scratch, int* total) 
 }
 
 // Bounded spin (lane-local) until *w >= target; false if it gave up.
-__device__ __forceinline__ bool spin_until_ge(volatile int* w, int target, volatile int* fail) {
+__device__ __forceinline__ bool spin_until_ge(volatile int* w, int target, volatile int* fail,
+                                              uint32_t limit) {
   uint32_t it = 0;
   while (*w < target) {
     if (*fail) return false;
-    if (++it > kSpinLimit) return false;
+    if (++it > limit) return false;
     __nanosleep(32);
   }
   return true;
@@ -726,7 +731,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
         }
         // the ring entry is free once its previous index (same consumer) has
         // been read
-        if (j >= MR && !spin_until_ge(vmisc + kMiscCons + kk, j - MR + 1, vmisc + kMiscFail)) {
+        if (j >= MR && !spin_until_ge(vmisc + kMiscCons + kk, j - MR + 1, vmisc + kMiscFail, a.wait_polls)) {
           vmisc[kMiscFail] = 1;
           set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
         }
@@ -767,7 +772,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   auto issue = [&](int q) -> bool {
     const int j = k + q * NC;
     if (q < nmine) {
-      if (lane == 0 && !spin_until_ge(vmisc + kMiscProd, j + 1, vmisc + kMiscFail)) {
+      if (lane == 0 && !spin_until_ge(vmisc + kMiscProd, j + 1, vmisc + kMiscFail, a.wait_polls)) {
         vmisc[kMiscFail] = 1;
         set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
       }
@@ -828,7 +833,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     const T* qp;
     if (h - hlo < nq) {
       if (!q_staged) {
-        if (!mbar_wait_bounded(qbar, 0)) {
+        if (!mbar_wait_bounded(qbar, 0, a.wait_polls)) {
           vmisc[kMiscFail] = 1;
           set_dev_error(a.dev_err, CVSA_DEV_ERR_TIMEOUT);
           return false;
@@ -1346,6 +1351,7 @@ cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendP
   a.acc1 = p.acc1;
   a.cov1 = p.cov1;
   a.scale = 1.0f / sqrtf((float)kv.d);
+  a.wait_polls = wait_limit() ? wait_limit() : kSpinLimit;
   int chunk = chunk_heads(q, kv, p.dense ? 1 : max_sel);
   if (chunk > heads) chunk = heads;
   const PartialLayout L = partial_layout(q, kv, chunk);

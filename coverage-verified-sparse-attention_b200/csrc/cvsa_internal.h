@@ -34,6 +34,9 @@ struct QView {
 
 int num_sms();
 int dtype_bytes(int dtype);
+// Polls a kernel's bounded waits on other warps make before giving up with
+// CVSA_DEV_ERR_TIMEOUT (cvsa_set_wait_limit); 0 = each kernel's default.
+uint32_t wait_limit();
 
 // Every workspace starts with a fixed region of counters that must be zero
 // when a kernel starts and that the kernels return to zero: per-(b, kv head)

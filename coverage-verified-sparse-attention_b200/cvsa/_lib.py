@@ -106,6 +106,7 @@ _SIGS = {
     "cvsa_decode_step": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc),
                           ctypes.POINTER(StepConfig), ctypes.POINTER(StepIO), _P, ctypes.c_size_t,
                           _P], ctypes.c_int),
+    "cvsa_set_wait_limit": ([ctypes.c_uint32], ctypes.c_int),
     "cvsa_workspace_reset": ([_P, ctypes.c_size_t, _P], ctypes.c_int),
     "cvsa_step_decision_word": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "cvsa_paged_append": ([ctypes.POINTER(KvDesc), _P, _P, _I, _P, _P, _I, _P, _P, _P, _I, _P, _P,

@@ -342,6 +342,16 @@ int cvsa_workspace_reset(void* workspace, size_t workspace_bytes, void* stream);
  * between CVSA_PHASE_SELECT and CVSA_PHASE_ATTEND (backend.py:446). */
 int cvsa_step_decision_word(void* workspace, int32_t** word);
 
+/* Polls a kernel's bounded waits on other warps of its CTA make before it
+ * gives up, records CVSA_DEV_ERR_TIMEOUT in the step's error word and returns
+ * without writing its outputs; 0 (the default) restores each kernel's own
+ * limit (about 4M polls). Applies to launches made after the call, by every
+ * host thread (a captured launch keeps the value it was captured with). It
+ * exists so a test can make the waits run out; after a timeout the
+ * workspace's counters may be left non-zero, so reset the workspace
+ * (cvsa_workspace_reset) before its next use. Not in the reference. */
+int cvsa_set_wait_limit(uint32_t polls);
+
 /* ---- paged KV runtime (cvsa/runtime/kv_cache.py) -------------------- */
 
 /* Append one token's K/V [batch, num_kv_heads, head_dim] (kv dtype) for each

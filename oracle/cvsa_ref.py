@@ -810,3 +810,63 @@ def topk_gap(page_scores: torch.Tensor, context_lens: torch.Tensor, block_size: 
             vals = sorted((float(page_scores[b, h, p]) for p in cand), reverse=True)
             gap[b, h] = vals[budget - 1] - vals[budget]
     return gap
+
+
+# --------------------------------------------------------------------------
+# paged KV runtime (cvsa/runtime/kv_cache.py:24-150)
+# --------------------------------------------------------------------------
+
+class PagedKVRef:
+    """CPU restatement of PagedKVCache + SequenceKVManager
+    (cvsa/runtime/kv_cache.py:24-150): a pool [num_blocks, block_size, H, D]
+    with a bump allocator (blocks handed out in order, kv_cache.py:53-62),
+    per-sequence block tables and context lengths; prefill writes whole
+    pages (:110-128), a decode append takes a new block when its token starts
+    a page past the ones allocated (:130-150)."""
+
+    def __init__(self, num_blocks, block_size, num_kv_heads, head_dim, dtype, batch_size,
+                 max_context_len):
+        self.bs = block_size
+        self.k = torch.zeros(num_blocks, block_size, num_kv_heads, head_dim, dtype=dtype)
+        self.v = torch.zeros_like(self.k)
+        self.next_free = 0
+        self.total = num_blocks
+        self.max_pages = (max_context_len + block_size - 1) // block_size
+        self.block_tables = torch.zeros(batch_size, self.max_pages, dtype=torch.int32)
+        self.context_lens = torch.zeros(batch_size, dtype=torch.int32)
+        self.pages = [0] * batch_size
+
+    def allocate(self, n):
+        assert self.next_free + n <= self.total, "Out of blocks"
+        ids = list(range(self.next_free, self.next_free + n))
+        self.next_free += n
+        return ids
+
+    def prefill(self, b, k_all, v_all):
+        n_tok = k_all.shape[0]
+        n_pages = (n_tok + self.bs - 1) // self.bs
+        ids = self.allocate(n_pages)
+        for p, blk in enumerate(ids):
+            self.block_tables[b, p] = blk
+            t0, t1 = p * self.bs, min((p + 1) * self.bs, n_tok)
+            self.k[blk, :t1 - t0] = k_all[t0:t1]
+            self.v[blk, :t1 - t0] = v_all[t0:t1]
+        self.context_lens[b] = n_tok
+        self.pages[b] = n_pages
+
+    def append(self, b, k, v):
+        pos = int(self.context_lens[b])
+        page, off = pos // self.bs, pos % self.bs
+        if off == 0 and page >= self.pages[b]:
+            self.block_tables[b, page] = self.allocate(1)[0]
+            self.pages[b] += 1
+        blk = int(self.block_tables[b, page])
+        self.k[blk, off] = k
+        self.v[blk, off] = v
+        self.context_lens[b] += 1
+
+    def gather(self, blocks):
+        """Dense [n * block_size, H, D] copies of the given blocks' K and V."""
+        idx = torch.as_tensor(blocks, dtype=torch.long)
+        return (self.k[idx].reshape(-1, *self.k.shape[2:]),
+                self.v[idx].reshape(-1, *self.v.shape[2:]))
