@@ -4,9 +4,10 @@ The ranks of a page split (each holding a contiguous range of every
 sequence's pages) run PageSplitBackend with the CUDA kernels; their step
 generators are driven in lockstep, each exchange served by stacking the
 ranks' tensors -- what all_gather returns. Every rank's output must match
-CVSABackend over the whole context within the bf16 bar, and the ranks'
-cached selections, mapped back to global pages, must together be its cached
-selection, across a lazy schedule with rescoring and reuse steps.
+the oracle (OracleBackend over the whole context, CPU) and CVSABackend within
+the bf16 bar, and the ranks' cached selections, mapped back to global pages,
+must together be the oracle's cached selection, across a lazy schedule with
+rescoring and reuse steps.
 """
 
 import pytest
@@ -15,6 +16,7 @@ import torch
 from cvsa import synthetic
 from cvsa.backend import CVSABackend
 from cvsa.pagesplit import PageSplitBackend, page_range, shard_sequence
+from oracle import cvsa_ref as R
 
 pytestmark = pytest.mark.gpu
 
@@ -49,6 +51,7 @@ def test_page_split_matches_one_gpu(cuda, world):
     kw = dict(num_layers=1, budget_pct=0.05, coverage_threshold=0.9, lazy=True,
               check_interval=2, sink_pages=1, local_pages=2)
     full = CVSABackend(8, 32, 128, 16, **kw)
+    ob = R.OracleBackend(8, 32, 128, 16, **kw)
     ranks = []
     nv = (wl.context_lens.long() + 15) // 16
     for r in range(world):
@@ -60,11 +63,14 @@ def test_page_split_matches_one_gpu(cuda, world):
     for step in range(6):
         q = (wl.q.float() + 0.6 * torch.randn(wl.q.shape, generator=g)).to(wl.q.dtype).to(cuda)
         ref = full(q, d.k_cache, d.v_cache, d.block_tables, d.context_lens, 0)
+        oref = ob(q.cpu(), wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+        _check_close(ref.cpu(), oref, step)
         outs = _lockstep([pb.step(q, k, v, bt, cl, 0, d.context_lens, d.block_tables.shape[1])
                           for pb, k, v, bt, cl, _ in ranks])
         for out in outs:
             _check_close(out, ref, step)
-        fi, fn = full.cached_selection(0)
+            _check_close(out.cpu(), oref, step)
+        fi, fn = ob._cached[0]
         for b in range(2):
             for h in range(8):
                 union = []
@@ -73,6 +79,7 @@ def test_page_split_matches_one_gpu(cuda, world):
                     union += [p + int(lo[b]) for p in li[b, h, :int(ln[b, h])].tolist()]
                 assert union == fi[b, h, :int(fn[b, h])].tolist(), (step, b, h)
         full.step_done(0, 1)
+        ob.step_done(0, 1)
         for pb, *_ in ranks:
             pb.step_done(0, 1)
 
