@@ -1008,6 +1008,82 @@ def run_cvsa(args, ws, rank, local):
         print(json.dumps(line), flush=True)
 
 
+KERNEL_CASES = ("select_warp", "select_big", "quest", "score_general", "attend_general",
+                "page_lse", "rank_merge", "append", "gather", "config3_step")
+
+
+def run_kernel_case(name: str, reps: int = 3):
+    """One kernel on a small fixed workload, `reps` launches (the ncu capture
+    targets of profiles/: `ncu -k regex:<kernel> -c 1 python bench.py
+    --kernel-case <name>`). Inputs are sized above L2 where the kernel reads
+    the KV pool."""
+    from cvsa import synthetic
+    from cvsa.kernels import coverage as C
+    from cvsa.kernels import page_scores as PS
+    from cvsa.kernels import select as SEL
+    from cvsa.kernels import sparse_decode as SD
+    dev = torch.device("cuda", 0)
+    if name in ("select_warp", "quest"):
+        wl = synthetic.config2(device=dev, seed=1000, gen_device=str(dev))
+    elif name in ("select_big", "config3_step"):
+        wl = synthetic.config3(device=dev, seed=3000, gen_device=str(dev))
+    elif name in ("score_general", "attend_general"):
+        # fp32 pool: the general-layout kernels (score_pages_kernel, attend_kernel)
+        wl = synthetic.small(device="cpu", seed=2, B=16, Hq=32, Hkv=8, D=128,
+                             ctx=(8192,) * 16, dtype=torch.float32).to(dev)
+    else:
+        wl = synthetic.small(device="cpu", seed=2, B=8, Hq=32, Hkv=8, D=128,
+                             ctx=(8192,) * 8).to(dev)
+    if name == "config3_step":
+        # one config-3 layer through the backend: a scoring step (score,
+        # selection over 8192 pages, attention with recovery) then reuse steps
+        from cvsa.backend import CVSABackend
+        be = CVSABackend(wl.num_kv_heads, wl.q.shape[1], 128, 16, num_layers=1,
+                         budget_pct=0.05, coverage_threshold=0.9, lazy=True, check_interval=4,
+                         sink_pages=1, local_pages=2)
+        for _ in range(reps + 1):
+            be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
+            be.step_done(0, 1)
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel_case": name, "reps": reps}), flush=True)
+        return
+    H, G = wl.num_kv_heads, wl.num_q_per_kv
+    W = wl.block_tables.shape[1]
+    scores = PS.score_pages(wl.q, wl.k_cache, wl.block_tables, wl.context_lens, H, G, 16)
+    budget = SEL.budget_for(W, 0.05)
+    idx, n = SEL.select_pages(scores, wl.context_lens, 16, budget, 1, 2)
+    torch.cuda.synchronize()
+    for _ in range(reps):
+        if name in ("select_warp", "select_big"):
+            SEL.select_pages(scores, wl.context_lens, 16, budget, 1, 2)
+        elif name == "quest":
+            PS.quest_page_scores(wl.q, wl.k_cache, wl.block_tables, wl.context_lens, H)
+        elif name == "score_general":
+            PS.score_pages(wl.q, wl.k_cache, wl.block_tables, wl.context_lens, H, G, 16)
+        elif name == "attend_general":
+            SD.sparse_decode(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, idx, n,
+                             wl.context_lens, H, G, 16)
+        elif name == "page_lse":
+            C.page_lse(scores, idx, n)
+        elif name == "rank_merge":
+            B, Hq, D = wl.q.shape
+            parts = torch.randn((8, B * Hq * (D + 2)), device=dev)
+            C.rank_merge(parts, B, H, G, D, torch.empty_like(wl.q))
+        elif name == "append":
+            from cvsa.runtime.kv_cache import PagedKVCache, SequenceKVManager
+            cache = PagedKVCache(64 * 64, 16, 8, 128, device="cuda")
+            mgr = SequenceKVManager(cache, 64, 4096)
+            kn = torch.randn((64, 8, 128), device=dev, dtype=torch.bfloat16)
+            for _t in range(16):
+                mgr.append_batch(kn, kn)
+        elif name == "gather":
+            from cvsa.runtime.kv_cache import PagedKVCache
+            cache = PagedKVCache(4096, 16, 8, 128, device="cuda")
+            cache.gather_pages(torch.randperm(4096, device=dev)[:2048])
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": name, "reps": reps}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1021,7 +1097,12 @@ def main():
                     help="skip the config-4 (70B, KV heads sharded over the GPUs) measurement")
     ap.add_argument("--no-c5", action="store_true",
                     help="skip the config-5 (ragged batch with appends) measurement")
+    ap.add_argument("--kernel-case", choices=KERNEL_CASES, default=None,
+                    help="run one kernel on a small fixed case (profiling target), no bench line")
     args = ap.parse_args()
+    if args.kernel_case:
+        run_kernel_case(args.kernel_case)
+        return
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         ws = int(os.environ.get("WORLD_SIZE", "1"))
