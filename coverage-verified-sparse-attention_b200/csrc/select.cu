@@ -720,7 +720,8 @@ __global__ void __launch_bounds__(NT) select_gate_kernel(SelectParams p) {
 }
 
 // ---------------------------------------------------------------------------
-// CTA of 1024 threads per (b, h): long tables (1024 < W <= 16384)
+// CTA of NT threads per (b, h): tables of 257 to 16384 pages (NT = 128 up to
+// 1024 pages, 1024 above)
 // ---------------------------------------------------------------------------
 // Thread t holds the EPT contiguous pages [t * EPT, (t + 1) * EPT) in
 // registers, so every block scan is in page order. The kernel is built from
@@ -738,18 +739,18 @@ __global__ void __launch_bounds__(NT) select_gate_kernel(SelectParams p) {
 // A bin too crowded to rank directly (heavy ties), or a candidate range that
 // is not finite, falls back to a radix select of the k-th key (4 bits per
 // pass over a packed 16-bin digit histogram) and a scan of the equal keys.
-constexpr int kBigNT = 1024;
-constexpr int kBigBins = 2048;   // = 2 * kBigNT
-constexpr int kBigBinCap = 256;  // bin entries ranked directly
+constexpr int kBigNT = 1024;    // threads of the long-table variant (bins: 2 per thread;
+                                // bin entries ranked directly: min(threads, 256))
 
 __device__ __forceinline__ float key_float(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-template <int EPT>
-__global__ void __launch_bounds__(kBigNT) select_gate_big_kernel(SelectParams p) {
-  constexpr int NT = kBigNT, NW = NT / 32;
-  static_assert(kBigBins == 2 * NT, "two bins per thread");
+template <int EPT, int NT>
+__global__ void __launch_bounds__(NT) select_gate_big_kernel(SelectParams p) {
+  constexpr int NW = NT / 32;
+  constexpr int kBigBins = 2 * NT;                      // two bins per thread
+  constexpr int kBigBinCap = NT < 256 ? NT : 256;       // one thread ranks one entry
   __shared__ uint32_t s_kred[NW][6];
   __shared__ float s_fred[NW][2];
   __shared__ int s_hist[kBigBins];
@@ -1126,9 +1127,9 @@ __global__ void __launch_bounds__(kBigNT) select_gate_big_kernel(SelectParams p)
   finish_select<NT>(p, tid == 0 ? rejects : 0, s_flag, wsum);
 }
 
-template <int EPT>
+template <int EPT, int NT = kBigNT>
 cudaError_t launch_sel_big(const SelectParams& p, cudaStream_t s, bool pdl) {
-  return launch_k(select_gate_big_kernel<EPT>, dim3(p.B * p.hkv), dim3(kBigNT), 0, s, pdl, p);
+  return launch_k(select_gate_big_kernel<EPT, NT>, dim3(p.B * p.hkv), dim3(NT), 0, s, pdl, p);
 }
 
 template <int NT>
@@ -1248,8 +1249,10 @@ cudaError_t launch_build_bitmap(const int32_t* idx, int max_sel, const int32_t* 
 cudaError_t launch_select_gate(const SelectParams& p, cudaStream_t s, bool pdl) {
   if (p.W <= 128) return launch_sel_warp<4>(p, s, pdl);
   if (p.W <= 256) return launch_sel_warp<8>(p, s, pdl);
-  if (p.W <= 512) return launch_sel_warp<16>(p, s, pdl);
-  if (p.W <= 1024) return launch_sel_warp<32>(p, s, pdl);
+  // 257..1024 pages: a CTA of 128 threads per head (4 times the warps of one
+  // warp per head, so the block steps' latency is shared among more warps)
+  if (p.W <= 512) return launch_sel_big<4, 128>(p, s, pdl);
+  if (p.W <= 1024) return launch_sel_big<8, 128>(p, s, pdl);
   if (p.W <= 4096) return launch_sel_big<4>(p, s, pdl);
   if (p.W <= 8192) return launch_sel_big<8>(p, s, pdl);
   if (p.W <= 16384) return launch_sel_big<16>(p, s, pdl);
