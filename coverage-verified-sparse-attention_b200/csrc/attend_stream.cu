@@ -118,7 +118,7 @@ struct StreamArgs {
   int h_base, n_heads; // heads [h_base, h_base + n_heads) of this launch
   int nc, stages, meta_cap;
   // shared-memory carve-up, byte offsets from the 1024-aligned base
-  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc, off_bnd;
   // the query rows of a CTA's first q_slots heads are copied into shared
   // memory at the start (one bulk copy per head on the mbarrier at off_qbar)
   int off_qbar, off_q, q_slots;
@@ -135,7 +135,9 @@ constexpr int kMiscProd = 5;       // page descriptors published (local position
 constexpr int kMiscScan = 8;       // [33] block-scan scratch
 constexpr int kMiscCons = 48;      // [kMaxConsumers] next position each consumer reads
 constexpr int kMiscWon = 56;       // [2] this CTA merges its first / last head
+constexpr int kMiscWmax = 58;      // the largest w_h of the launch
 constexpr int kMiscWords = 64;
+constexpr int kMaxBnd = 256;       // CTAs of a launch whose ranges may snap to head starts
 
 // Consumer warps a launch may use: 8, or 4 where the wider per-lane state
 // (head_dim 256, or more than 8 query heads at head_dim 128) needs the larger
@@ -514,7 +516,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   {
     const int per = (H + nthreads - 1) / nthreads;
     const int h0 = min(tid * per, H), h1 = min(h0 + per, H);
-    int sum = 0;
+    int sum = 0, wmx = 0;
     long long att = 0, mx = 0;
     const int src = a.src_select == 2 ? ((dec & 1) ? 0 : 1) : a.src_select;
     for (int h = h0; h < h1; ++h) {
@@ -553,6 +555,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
       kindv[h] = (uint8_t)kind;
       pref[h] = w;
       sum += w;
+      wmx = max(wmx, w);
     }
     if (c == 0 && a.counters) {
 #pragma unroll
@@ -569,6 +572,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
     }
     int total = 0;
     int base = block_excl_scan(sum, misc + kMiscScan, &total);
+    if (wmx > 0) atomicMax(&misc[kMiscWmax], wmx);   // (misc is zeroed: the scan synced)
     for (int h = h0; h < h1; ++h) {
       const int w = pref[h];
       pref[h] = base;
@@ -602,14 +606,48 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
   };
 
   const int P = pref[H];
-  const int Xc = (int)((long long)P * c / C);
-  const int Xe = (int)((long long)P * (c + 1) / C);
+  // CTA c holds the stream positions [bnd[c], bnd[c + 1]): the equal cuts
+  // P c / C or, when no head is longer than a CTA's share (reuse steps: short
+  // selections), those cuts moved to the nearest head start, so that no head
+  // is split over CTAs and the launch needs no cross-CTA merge (streaming is
+  // HBM-bound, so the uneven shares cost little)
+  int* bnd = reinterpret_cast<int*>(sm + a.off_bnd);
+  const bool aligned = P > 0 && C <= kMaxBnd && (long long)misc[kMiscWmax] * C <= P;
+  if (aligned) {
+    for (int i = tid; i <= C; i += nthreads) {
+      const int x = (int)((long long)P * i / C);
+      int bi = x;
+      if (i > 0 && i < C) {
+        int lo = 0, hi = H - 1;  // largest h with pref[h] <= x
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (pref[mid] <= x) lo = mid;
+          else hi = mid - 1;
+        }
+        const int s0 = pref[lo], s1 = pref[lo + 1];
+        bi = (x - s0 <= s1 - x) ? s0 : s1;
+      }
+      bnd[i] = bi;
+    }
+    __syncthreads();
+  }
+  const int Xc = aligned ? bnd[c] : (int)((long long)P * c / C);
+  const int Xe = aligned ? bnd[c + 1] : (int)((long long)P * (c + 1) / C);
   const int nloc = Xe - Xc;
   // first / last CTA that works on each head (an empty head belongs to the
-  // CTA holding its position), computed once: CTA c holds stream positions
-  // [P c / C, P (c + 1) / C), so position x lies in CTA ((x + 1) C - 1) / P
+  // CTA holding its position), computed once: position x lies in the last
+  // CTA whose range starts at or before it (((x + 1) C - 1) / P for equal cuts)
   {
-    auto cta_of = [&](int x) -> int { return (int)(((long long)(x + 1) * C - 1) / P); };
+    auto cta_of = [&](int x) -> int {
+      if (!aligned) return (int)(((long long)(x + 1) * C - 1) / P);
+      int lo = 0, hi = C - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (bnd[mid] <= x) lo = mid;
+        else hi = mid - 1;
+      }
+      return lo;
+    };
     for (int h = tid; h < H; h += nthreads) {
       const int s0 = pref[h], w = pref[h + 1] - s0;
       const int f = s0 < P ? cta_of(s0) : C - 1;
@@ -1135,7 +1173,7 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
 // ---------------------------------------------------------------------------
 struct Plan {
   int nc, stages, meta_cap, smem;
-  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc;
+  int off_meta, off_snt, off_pref, off_ctx, off_kind, off_span, off_misc, off_bnd;
 };
 
 size_t up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -1152,7 +1190,8 @@ bool make_plan(int D, int n_heads, int max_nc, Plan* best) {
     const int meta_cap = kMetaPerConsumer * nc;
     const size_t tail = up((size_t)meta_cap * 8, 16) + up((size_t)nc * kMaxStages * 4, 16) +
                         up((size_t)(n_heads + 1) * 4, 16) + up((size_t)n_heads * 4, 16) +
-                        up((size_t)n_heads, 16) + up((size_t)n_heads * 4, 16) + kMiscWords * 4;
+                        up((size_t)n_heads, 16) + up((size_t)n_heads * 4, 16) + kMiscWords * 4 +
+                        up((size_t)(kMaxBnd + 1) * 4, 16);
     const size_t avail = (size_t)kSmemCap - 1024;  // alignment slack of the dynamic base
     if (avail <= tail) continue;
     int stages = (int)((avail - tail) / (stage * nc));
@@ -1166,6 +1205,7 @@ bool make_plan(int D, int n_heads, int max_nc, Plan* best) {
     p.off_kind = (int)off; off += up((size_t)n_heads, 16);
     p.off_span = (int)off; off += up((size_t)n_heads * 4, 16);
     p.off_misc = (int)off; off += kMiscWords * 4;
+    p.off_bnd = (int)off; off += up((size_t)(kMaxBnd + 1) * 4, 16);
     if (off + 1024 > (size_t)kSmemCap) continue;
     p.nc = nc;
     p.stages = stages;
@@ -1197,6 +1237,7 @@ cudaError_t launch_typed(StreamArgs& a, cudaStream_t s, bool pdl) {
   a.off_kind = pl.off_kind;
   a.off_span = pl.off_span;
   a.off_misc = pl.off_misc;
+  a.off_bnd = pl.off_bnd;
   // query-row staging in the shared memory the plan leaves over
   {
     const size_t qbytes = (size_t)a.G * D * sizeof(T);
