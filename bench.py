@@ -683,12 +683,15 @@ def measure_config5(dev, warmup, ws, rank):
             "launch": "CUDA graphs: append, lazy-check step, reuse step"}
 
 
-# DRAM bytes (read + write) per launch from the ncu captures of the config-2
-# bench workload (profiles/stream_attend_config2.md, score_stream_config2.md):
-# the lazy-check launch and the reuse launch of stream_attend_kernel, and the
-# scoring launch. The roofline entries scale them to the launch mix timed.
-NCU_TRAFFIC = {"attend_check": 233.66e6 + 3.75e6, "attend_reuse": 59.20e6 + 1.32e6,
-               "score": 537.30e6 + 3.75e6}
+# DRAM bytes (read + write) per algorithmic byte of each launch kind, from the
+# ncu captures of the config-2 bench workload (profiles/stream_attend_config2.md,
+# profiles/score_stream_config2.md): a launch's traffic is this ratio times the
+# algorithmic bytes of the same launch kind in this run (traffic grows with the
+# pages a launch reads; the captured launches' own rejection mix differs from a
+# given run's).
+NCU_TRAFFIC_RATIO = {"attend_check": (233.66e6 + 3.54e6) / 233.2e6,
+                     "attend_reuse": (59.17e6 + 0.76e6) / 58.7e6,
+                     "score": (537.30e6 + 3.75e6) / 536.87e6}
 
 
 def roofline_table(kern, att_pages, layers, score_bytes, peak, peak_kind):
@@ -709,14 +712,16 @@ def roofline_table(kern, att_pages, layers, score_bytes, peak, peak_kind):
         launches = n_check + n_reuse
         avg_bytes = (n_check * b_check + n_reuse * b_reuse) / launches
         avg_ms = (n_check * t_check + n_reuse * t_reuse) / launches
-        traffic = (n_check * NCU_TRAFFIC["attend_check"]
-                   + n_reuse * NCU_TRAFFIC["attend_reuse"]) / launches
+        traffic = (n_check * NCU_TRAFFIC_RATIO["attend_check"] * b_check
+                   + n_reuse * NCU_TRAFFIC_RATIO["attend_reuse"] * b_reuse) / launches
         out.append(dict(kernel="stream_attend_kernel", launch="cycle mean (1 check + "
                         f"{n_reuse} reuse launches)", time_ms_per_cycle=avg_ms * launches,
                         algorithmic_bytes_per_launch=avg_bytes, avg_launch_ms=avg_ms,
                         traffic=traffic))
-        for name, b, t, tr in (("check", b_check, t_check, NCU_TRAFFIC["attend_check"]),
-                               ("reuse", b_reuse, t_reuse, NCU_TRAFFIC["attend_reuse"])):
+        for name, b, t, tr in (("check", b_check, t_check,
+                                NCU_TRAFFIC_RATIO["attend_check"] * b_check),
+                               ("reuse", b_reuse, t_reuse,
+                                NCU_TRAFFIC_RATIO["attend_reuse"] * b_reuse)):
             out.append(dict(kernel="stream_attend_kernel", launch=name,
                             time_ms_per_cycle=t * (n_check if name == "check" else n_reuse),
                             algorithmic_bytes_per_launch=b, avg_launch_ms=t, traffic=tr))
@@ -724,10 +729,12 @@ def roofline_table(kern, att_pages, layers, score_bytes, peak, peak_kind):
         t = mean(kern["score"])
         out.append(dict(kernel="score_stream_kernel", launch="check", time_ms_per_cycle=t,
                         algorithmic_bytes_per_launch=score_bytes, avg_launch_ms=t,
-                        traffic=NCU_TRAFFIC["score"]))
+                        traffic=NCU_TRAFFIC_RATIO["score"] * score_bytes))
     if kern["select"]:
         t = mean(kern["select"])
-        out.append(dict(kernel="select_gate_warp_kernel", launch="check", time_ms_per_cycle=t,
+        # the kernel the selection dispatch picks for config 2's 512-page tables
+        out.append(dict(kernel="select_gate_big_kernel<4, 128>", launch="check",
+                        time_ms_per_cycle=t,
                         algorithmic_bytes_per_launch=0, avg_launch_ms=t, traffic=None,
                         note="reads 0.5 MB of page scores from L2; latency-bound"))
     for r in out:
