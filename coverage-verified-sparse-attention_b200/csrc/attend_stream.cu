@@ -138,6 +138,11 @@ constexpr int kMiscWon = 56;       // [2] this CTA merges its first / last head
 constexpr int kMiscWmax = 58;      // the largest w_h of the launch
 constexpr int kMiscWords = 64;
 constexpr int kMaxBnd = 256;       // CTAs of a launch whose ranges may snap to head starts
+// Longest head (pages) for which the ranges snap to head starts: a snapped cut
+// moves by at most half a head, <= 16 page-heads (about 3 us of one SM's share
+// of HBM), about the cross-CTA merge it saves; longer heads (ragged batches,
+// long selections) keep equal cuts, where the shift would unbalance the CTAs
+constexpr int kAlignMaxW = 32;
 
 // Consumer warps a launch may use: 8, or 4 where the wider per-lane state
 // (head_dim 256, or more than 8 query heads at head_dim 128) needs the larger
@@ -607,12 +612,14 @@ stream_attend_kernel(const __grid_constant__ StreamArgs a) {
 
   const int P = pref[H];
   // CTA c holds the stream positions [bnd[c], bnd[c + 1]): the equal cuts
-  // P c / C or, when no head is longer than a CTA's share (reuse steps: short
-  // selections), those cuts moved to the nearest head start, so that no head
-  // is split over CTAs and the launch needs no cross-CTA merge (streaming is
-  // HBM-bound, so the uneven shares cost little)
+  // P c / C or, when every head is short (at most kAlignMaxW pages and a CTA's
+  // share: reuse steps with short selections), those cuts moved to the nearest
+  // head start, so that no head is split over CTAs and the launch needs no
+  // cross-CTA merge
   int* bnd = reinterpret_cast<int*>(sm + a.off_bnd);
-  const bool aligned = P > 0 && C <= kMaxBnd && (long long)misc[kMiscWmax] * C <= P;
+  const int wmax = misc[kMiscWmax];
+  const bool aligned = P > 0 && C <= kMaxBnd && wmax <= kAlignMaxW &&
+                       (long long)wmax * C <= P;
   if (aligned) {
     for (int i = tid; i <= C; i += nthreads) {
       const int x = (int)((long long)P * i / C);
