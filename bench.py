@@ -489,9 +489,10 @@ C3S_LAYERS = 4
 
 def measure_config3_split(dev, steps, ws, rank):
     """Config 3 (one 128K sequence) with its pages split over the ranks
-    (cvsa.pagesplit): every rank scores, selects and attends its contiguous
-    page range; proposals, partials and coverage sums are all-gathered (NCCL)
-    and merged in rank order. Lazy M=4 over C3S_LAYERS layers; the lazy-check
+    (cvsa.pagesplit): every rank scores, proposes and attends its contiguous
+    page range; the proposal rows (candidates and coverage sums) and the
+    attention partials are all-gathered (NCCL, two per lazy-check step, one
+    per reuse step) and merged in rank order. Lazy M=4 over C3S_LAYERS layers; the lazy-check
     step and the reuse step (all layers each) are captured as CUDA graphs with
     the all-gathers inside and timed separately; times are the max over
     ranks."""
@@ -578,13 +579,64 @@ def measure_config3_split(dev, steps, ws, rank):
         res[kind] = _max_over_ranks(e0.elapsed_time(e1), ws) * 1e3 / (n * C3S_LAYERS)
     del graphs
     us_layer = (res["check"] + (M_INTERVAL - 1) * res["reuse"]) / M_INTERVAL
+    breakdown = _split_breakdown(pb, pools, ag, ws)
     return {"workload": "config3: B=1, Hq=32, Hkv=8, D=128, bf16, ctx=131072 (8192 pages), "
                         f"pages split contiguously over {ws} GPU(s), lazy M=4, {C3S_LAYERS} layers",
             "us_per_layer_lazy_check": res["check"], "us_per_layer_reuse": res["reuse"],
             "us_per_layer": us_layer, "steps_per_kind": n,
             "launch": ("CUDA graph per step kind (NCCL all-gathers inside)" if ok else
                        "eager (graph capture of the collectives failed)"),
+            "breakdown_us_per_layer": breakdown,
             "stats_rank0_warmup": stats}
+
+
+def _split_breakdown(pb, pools, ag, ws):
+    """Per-op device time of one eager lazy-check step and one eager reuse
+    step of the page split (CUDA events around every kernel call and every
+    all-gather on the current stream; max over ranks, per layer). The events
+    separate the launches (no overlap), so the sum exceeds the graph-replayed
+    step."""
+    import types
+    from cvsa.pagesplit import run_step
+
+    names = ("score_pages", "split_propose", "split_gate", "split_attend", "decode_unnorm",
+             "rank_merge")
+    records = []
+
+    def wrap(label, fn):
+        def call(*a, **k):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            r = fn(*a, **k)
+            e1.record()
+            records.append((label, e0, e1))
+            return r
+        return call
+
+    ops = pb.ops
+    pb.ops = types.SimpleNamespace(**{nm: wrap(nm, getattr(ops, nm)) for nm in names})
+    tag = wrap("all_gather", ag)
+    out = {}
+    try:
+        for kind, step_idx in (("check", 0), ("reuse", 1)):
+            records.clear()
+            pb._step = step_idx
+            # hold the stream (a fixed spin of about 25 ms) while the host
+            # enqueues the step, so no event pair spans host launch gaps
+            torch.cuda._sleep(50_000_000)
+            for l, (q, k, v, bt, cl, ctx, W) in enumerate(pools):
+                run_step(pb.step(q, k, v, bt, cl, l, ctx, W), tag)
+            torch.cuda.synchronize()
+            tot = {}
+            for label, e0, e1 in records:
+                tot[label] = tot.get(label, 0.0) + e0.elapsed_time(e1)
+            out[kind] = {label: _max_over_ranks(tot.get(label, 0.0), ws) * 1e3 / len(pools)
+                         for label in ("score_pages", "split_propose", "all_gather", "split_gate",
+                                       "split_attend", "decode_unnorm", "rank_merge")}
+    finally:
+        pb.ops = ops
+    return out
 
 
 C5_STEPS = 256

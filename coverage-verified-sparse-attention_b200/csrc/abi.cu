@@ -406,6 +406,169 @@ int cvsa_rank_accept(const float* parts, int32_t world, int64_t row_stride, int6
                      "rank_accept launch");
 }
 
+namespace {
+// Checks a split descriptor; rows = batch * num_kv_heads.
+int check_split(const cvsa_split_desc_t* sd, int64_t* rows) {
+  if (!sd) return fail(CVSA_ERR_INVALID, "NULL split descriptor");
+  if (sd->world <= 0 || sd->rank < 0 || sd->rank >= sd->world || sd->batch < 0 ||
+      sd->num_kv_heads <= 0 || sd->max_pages <= 0 || sd->block_size <= 0 || sd->budget < 0 ||
+      sd->max_sel <= 0 || sd->sink_pages < 0 || sd->local_pages < 0)
+    return fail(CVSA_ERR_INVALID, "bad split descriptor");
+  if (sd->budget + sd->sink_pages + sd->local_pages > sd->max_sel)
+    return fail(CVSA_ERR_INVALID, "max_sel < budget + sink_pages + local_pages");
+  if ((int64_t)sd->batch * sd->num_kv_heads > INT32_MAX / 2)
+    return fail(CVSA_ERR_INVALID, "too many heads");
+  *rows = (int64_t)sd->batch * sd->num_kv_heads;
+  return CVSA_OK;
+}
+}  // namespace
+
+int64_t cvsa_split_row_floats(const cvsa_split_desc_t* sd) {
+  int64_t rows;
+  if (check_split(sd, &rows)) return 0;
+  return rows * 3 + rows * sd->max_sel;
+}
+
+int cvsa_split_propose(const cvsa_split_desc_t* sd, const float* page_scores,
+                       const int32_t* context_lens, const int32_t* cached_indices,
+                       const int32_t* cached_n, float* exchange_row, int32_t* proposal_pages,
+                       void* stream) {
+  int64_t rows;
+  int st = check_split(sd, &rows);
+  if (st) return st;
+  if (rows == 0) return CVSA_OK;
+  if (!page_scores || !context_lens || !exchange_row || !proposal_pages)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  if ((cached_indices == nullptr) != (cached_n == nullptr))
+    return fail(CVSA_ERR_INVALID, "cached_indices and cached_n go together");
+  if (split_propose_smem(sd->max_pages) > 200 * 1024)
+    return fail(CVSA_ERR_UNSUPPORTED, "split_propose supports up to 51200 pages per rank");
+  SplitProposeParams p;
+  memset(&p, 0, sizeof(p));
+  p.scores = page_scores;
+  p.rows = (int)rows;
+  p.W = sd->max_pages;
+  p.H = sd->num_kv_heads;
+  p.lens = context_lens;
+  p.bs = sd->block_size;
+  p.cached_idx = cached_indices;
+  p.cached_n = cached_n;
+  p.cached_stride = sd->max_sel;
+  p.sink = sd->sink_pages;
+  p.local = sd->local_pages;
+  p.budget = sd->budget;
+  p.max_sel = sd->max_sel;
+  p.ex = exchange_row;
+  p.off_all = 0;
+  p.off_cached = rows;
+  p.off_forced = 2 * rows;
+  p.off_cand = 3 * rows;
+  p.prop_idx = proposal_pages;
+  return cuda_status(launch_split_propose(p, (cudaStream_t)stream, false), "split_propose launch");
+}
+
+int cvsa_split_gate(const cvsa_split_desc_t* sd, const float* exchange, int64_t row_stride,
+                    const int32_t* proposal_pages, const int32_t* context_lens,
+                    int32_t has_cache, int32_t stats_mode, int32_t* sel, int32_t* n_sel,
+                    uint8_t* accept, uint32_t* bitmap, int32_t* state, int64_t* counters,
+                    int32_t* dev_error, void* stream) {
+  int64_t rows;
+  int st = check_split(sd, &rows);
+  if (st) return st;
+  if (row_stride < rows * 3 + rows * sd->max_sel) return fail(CVSA_ERR_INVALID, "row_stride too small");
+  if (rows == 0) return CVSA_OK;
+  if (!exchange || !proposal_pages || !context_lens || !sel || !n_sel || !accept || !state)
+    return fail(CVSA_ERR_INVALID, "NULL pointer");
+  const int words = bitmap_words(sd->max_pages);
+  if (split_gate_smem(sd->world, sd->max_sel, words) > 200 * 1024)
+    return fail(CVSA_ERR_UNSUPPORTED, "world * max_sel too large for split_gate");
+  SplitGateParams p;
+  memset(&p, 0, sizeof(p));
+  p.parts = exchange;
+  p.world = sd->world;
+  p.rank = sd->rank;
+  p.stride = row_stride;
+  p.off_all = 0;
+  p.off_cached = rows;
+  p.off_forced = 2 * rows;
+  p.off_cand = 3 * rows;
+  p.rows = (int)rows;
+  p.H = sd->num_kv_heads;
+  p.max_sel = sd->max_sel;
+  p.budget = sd->budget;
+  p.tau = sd->tau;
+  p.prop_idx = proposal_pages;
+  p.lens = context_lens;
+  p.bs = sd->block_size;
+  p.W = sd->max_pages;
+  p.sink = sd->sink_pages;
+  p.local = sd->local_pages;
+  p.has_cache = has_cache ? 1 : 0;
+  p.stats_mode = stats_mode;
+  p.sel = sel;
+  p.n = n_sel;
+  p.acc = accept;
+  p.bitmap = bitmap;
+  p.bitmap_words = words;
+  p.state = state;
+  p.counters = counters;
+  p.dev_err = dev_error;
+  return cuda_status(launch_split_gate(p, (cudaStream_t)stream, false), "split_gate launch");
+}
+
+int cvsa_split_attend(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
+                      int32_t* cached_indices, int32_t* cached_n, const int32_t* sel,
+                      const int32_t* n_sel, int32_t max_sel, const int32_t* decision,
+                      const uint8_t* accept, const uint32_t* bitmap, float* o_unnorm, float* m,
+                      float* l, int32_t* dev_error, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  KvView kv;
+  QView q;
+  int st = check_kv(kvd, &kv);
+  if (st) return st;
+  st = check_q(qd, kv, true, &q);
+  if (st) return st;
+  if (max_sel <= 0) return fail(CVSA_ERR_INVALID, "max_sel must be positive");
+  if (!attend_supported(q, kv))
+    return fail(CVSA_ERR_UNSUPPORTED, "decode built for block_size 16, head_dim 64/128/256, G<=16");
+  if (!o_unnorm || !m || !l) return fail(CVSA_ERR_INVALID, "the partial outputs are required");
+  if (q.B == 0) return CVSA_OK;
+  if (!sel || !n_sel || !accept || !bitmap) return fail(CVSA_ERR_INVALID, "NULL selection");
+  if (decision && (!cached_indices || !cached_n))
+    return fail(CVSA_ERR_INVALID, "a decision needs the cached selection");
+  if ((cached_indices == nullptr) != (cached_n == nullptr))
+    return fail(CVSA_ERR_INVALID, "cached_indices and cached_n go together");
+  const size_t need = decode_ws(q, kv, max_sel);
+  if (!workspace || workspace_bytes < need || reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(CVSA_ERR_WORKSPACE, "workspace needs %zu bytes, 256-aligned", need);
+  AttendParams p;
+  memset(&p, 0, sizeof(p));
+  p.sel0 = cached_indices;
+  p.n0 = cached_n;
+  p.sel1 = sel;
+  p.n1 = n_sel;
+  p.sel_stride = max_sel;
+  p.src_select = decision ? 2 : 1;
+  p.decision = decision;
+  p.recover = true;
+  p.accept = accept;
+  p.bitmap = bitmap;
+  p.bitmap_words = bitmap_words(q.W);
+  p.commit_src1 = cached_indices != nullptr;
+  p.commit_idx = cached_indices;
+  p.commit_n = cached_n;
+  p.o_unnorm = o_unnorm;
+  p.m_out = m;
+  p.l_out = l;
+  p.dev_err = dev_error;
+  const DecodeLayout L = decode_layout(q, kv, max_sel);
+  p.partials = reinterpret_cast<uint8_t*>(workspace) + L.partials;
+  p.partial_bytes = L.partial_bytes;
+  p.head_done = ws_head_done(workspace);
+  return cuda_status(launch_attend(q, kv, p, max_sel, (cudaStream_t)stream, false),
+                     "split attend launch");
+}
+
 int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
                        const int32_t* page_indices, int32_t max_sel, const int32_t* n_per_head,
                        const uint8_t* accept, const float* o_d, const float* m_d, const float* l_d,

@@ -299,6 +299,37 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---------------------------------------------------------------------------
+// online log-sum-exp: (m, s) = (running max, sum of exp(x - m)); -inf
+// entries carry no mass, an empty pair is (-inf, 0)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
+  if (x == neg_inf()) return;
+  if (x > m) {
+    s = s * expf(m - x) + 1.f;
+    m = x;
+  } else {
+    s += expf(x - m);
+  }
+}
+
+// (m, s) pairs of the warp's lanes combined in place (every lane ends with
+// the warp's pair).
+__device__ __forceinline__ void lse_warp_pair(float& m, float& s) {
+  for (int o = 16; o > 0; o >>= 1) {
+    const float mo = __shfl_xor_sync(0xffffffffu, m, o);
+    const float so = __shfl_xor_sync(0xffffffffu, s, o);
+    const float M = fmaxf(m, mo);
+    if (M == neg_inf()) continue;
+    s = (m == neg_inf() ? 0.f : s * expf(m - M)) + (mo == neg_inf() ? 0.f : so * expf(mo - M));
+    m = M;
+  }
+}
+
+__device__ __forceinline__ float lse_value(float m, float s) {
+  return m == neg_inf() ? neg_inf() : m + logf(s);
+}
+
 __device__ __forceinline__ void set_dev_error(int32_t* err, int32_t bits) {
   if (err) atomicOr(err, bits);
 }

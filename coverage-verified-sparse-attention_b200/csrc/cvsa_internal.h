@@ -170,6 +170,45 @@ size_t stream_attend_workspace_bytes(const QView& q, const KvView& kv, int max_s
 cudaError_t launch_stream_attend(const QView& q, const KvView& kv, const AttendParams& p,
                                  int max_sel, cudaStream_t s, bool pdl);
 
+// ---- split.cu (page-split step: selection over ranks) ----
+struct SplitProposeParams {
+  const float* scores;          // [rows, W] this rank's page scores
+  int rows, W, H;               // rows = B * H
+  const int32_t* lens;          // [B] this rank's context lengths (tokens in its range)
+  int bs;
+  const int32_t* cached_idx;    // [rows, cached_stride] or null
+  const int32_t* cached_n;      // [rows]
+  int cached_stride;
+  int sink, local, budget, max_sel;
+  float* ex;                    // this rank's exchange-A row
+  int64_t off_all, off_cached, off_forced, off_cand;
+  int32_t* prop_idx;            // [rows, max_sel] local pages of the candidates
+};
+struct SplitGateParams {
+  const float* parts;           // [world, stride] gathered exchange-A rows
+  int world, rank;
+  int64_t stride, off_all, off_cached, off_forced, off_cand;
+  int rows, H, max_sel, budget;
+  float tau;
+  const int32_t* prop_idx;      // [rows, max_sel] this rank's candidates' pages
+  const int32_t* lens;          // [B] this rank's context lengths
+  int bs, W;                    // W = this rank's table width
+  int sink, local;              // this rank's forced pages
+  int has_cache;                // gate the cached selection (lazy check step)
+  int stats_mode;               // bit0: lazy check step, bit1: lazy mode
+  int32_t* sel; int32_t* n;     // [rows, max_sel], [rows] this rank's new selection
+  uint8_t* acc;                 // [rows] gate of the new selection
+  uint32_t* bitmap;             // [rows, bitmap_words] of the new selection, or null
+  int bitmap_words;             // >= ceil(W / 32)
+  int32_t* state;               // [4] zeroed once: tickets, two accept counts, decision word
+  int64_t* counters;            // [CVSA_SPLIT_NUM_COUNTERS] or null
+  int32_t* dev_err;
+};
+size_t split_propose_smem(int W);
+size_t split_gate_smem(int world, int max_sel, int bitmap_words);
+cudaError_t launch_split_propose(const SplitProposeParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_split_gate(const SplitGateParams& p, cudaStream_t s, bool pdl);
+
 // ---- merge.cu ----
 cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
                              const float* o_c, const float* m_c, const float* l_c,

@@ -92,33 +92,6 @@ __global__ void rank_merge_kernel(const float* __restrict__ parts, int world, in
 // (max, sum) per thread, combined across each warp and then across warps.
 constexpr int kLseThreads = 256;
 
-__device__ __forceinline__ void lse_push(float& m, float& s, float x) {
-  if (x == neg_inf()) return;
-  if (x > m) {
-    s = s * expf(m - x) + 1.f;
-    m = x;
-  } else {
-    s += expf(x - m);
-  }
-}
-
-// (m, s) pairs of the warp's lanes combined in place (every lane ends with
-// the warp's pair).
-__device__ __forceinline__ void lse_warp_pair(float& m, float& s) {
-  for (int o = 16; o > 0; o >>= 1) {
-    const float mo = __shfl_xor_sync(0xffffffffu, m, o);
-    const float so = __shfl_xor_sync(0xffffffffu, s, o);
-    const float M = fmaxf(m, mo);
-    if (M == neg_inf()) continue;
-    s = (m == neg_inf() ? 0.f : s * expf(m - M)) + (mo == neg_inf() ? 0.f : so * expf(mo - M));
-    m = M;
-  }
-}
-
-__device__ __forceinline__ float lse_value(float m, float s) {
-  return m == neg_inf() ? neg_inf() : m + logf(s);
-}
-
 __global__ void __launch_bounds__(kLseThreads)
 page_lse_kernel(const float* __restrict__ scores, int W, const int32_t* __restrict__ idx,
                 int max_sel, const int32_t* __restrict__ n, float* __restrict__ lse_all,

@@ -78,6 +78,15 @@ class StepIO(ctypes.Structure):
     ]
 
 
+class SplitDesc(ctypes.Structure):
+    _fields_ = [
+        ("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("batch", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32), ("max_pages", ctypes.c_int32),
+        ("block_size", ctypes.c_int32), ("budget", ctypes.c_int32), ("max_sel", ctypes.c_int32),
+        ("sink_pages", ctypes.c_int32), ("local_pages", ctypes.c_int32), ("tau", ctypes.c_float),
+    ]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _SIGS = {
@@ -98,6 +107,12 @@ _SIGS = {
     "cvsa_page_lse": ([_P, _I, _I, _P, _I, _P, _P, _P, _P], ctypes.c_int),
     "cvsa_rank_accept": ([_P, _I, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _I,
                           ctypes.c_float, _P, _P], ctypes.c_int),
+    "cvsa_split_row_floats": ([ctypes.POINTER(SplitDesc)], ctypes.c_int64),
+    "cvsa_split_propose": ([ctypes.POINTER(SplitDesc), _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "cvsa_split_gate": ([ctypes.POINTER(SplitDesc), _P, ctypes.c_int64, _P, _P, _I, _I, _P, _P,
+                         _P, _P, _P, _P, _P, _P], ctypes.c_int),
+    "cvsa_split_attend": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _P, _P, _P, _I,
+                           _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P], ctypes.c_int),
     "cvsa_rank_merge": ([_P, _I, ctypes.c_int64, _I, _I, _I, _I, _P, _P, _I, _P], ctypes.c_int),
     "cvsa_recover_merge": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P,
                             _P, _P, _P, _I, _P, ctypes.c_size_t, _P], ctypes.c_int),

@@ -220,6 +220,94 @@ int cvsa_page_lse(const float* page_scores, int32_t rows, int32_t max_pages,
 int cvsa_rank_accept(const float* parts, int32_t world, int64_t row_stride, int64_t off_all,
                      int64_t off_sel, int32_t rows, float tau, uint8_t* accept, void* stream);
 
+/* ---- page split: the scoring / lazy-check step over ranks ----------------
+ * Each rank (one process per GPU) holds a contiguous range of every
+ * sequence's pages. The scoring step of cvsa/backend.py:683-864 and the lazy
+ * check of :392-465 take two all-gathers per layer:
+ *   cvsa_score_pages -> cvsa_split_propose -> all-gather of the exchange rows
+ *   -> cvsa_split_gate -> cvsa_split_attend -> all-gather of the partials
+ *   -> cvsa_rank_merge.
+ * A reuse step (backend.py:866-881) is cvsa_sparse_decode of the cached
+ * selection into the partials, one all-gather, cvsa_rank_merge.
+ * Rank r's exchange row holds, for the rows = batch * num_kv_heads heads:
+ *   [0, rows)            lse_all_r    log-sum-exp of its pages' scores
+ *   [rows, 2 rows)       lse_cached_r of the cached selection's pages (-inf: none)
+ *   [2 rows, 3 rows)     lse_forced_r of its forced pages
+ *   [3 rows, 3 rows + rows * max_sel)  its best `budget` non-forced pages'
+ *                        scores per head, page order, -inf padded
+ * (cvsa_split_row_floats floats). */
+typedef struct cvsa_split_desc {
+  int32_t world;        /* ranks */
+  int32_t rank;         /* this rank (the all-gather's row order) */
+  int32_t batch;
+  int32_t num_kv_heads;
+  int32_t max_pages;    /* this rank's block-table width */
+  int32_t block_size;
+  int32_t budget;       /* top-k budget of the whole sequence (backend.py:690) */
+  int32_t max_sel;      /* >= budget + sink + local of the whole sequence */
+  int32_t sink_pages;   /* this rank's forced leading pages (rank 0: the sink) */
+  int32_t local_pages;  /* this rank's forced trailing pages (last rank: the window) */
+  float tau;            /* coverage threshold */
+} cvsa_split_desc_t;
+
+/* page-split step counters (int64 each), accumulated by cvsa_split_gate */
+enum {
+  CVSA_SPLIT_CTR_SCORING = 0,     /* scoring steps (backend.py _total_scoring_steps) */
+  CVSA_SPLIT_CTR_ACCEPT = 1,      /* lazy checks whose cached selection passed */
+  CVSA_SPLIT_CTR_REJECT = 2,      /* lazy checks that rescored */
+  CVSA_SPLIT_CTR_HEADS_ACC = 3,   /* heads accepted */
+  CVSA_SPLIT_CTR_CHECKS = 4,      /* coverage checks */
+  CVSA_SPLIT_CTR_HEADS_TOTAL = 5, /* heads gated */
+  CVSA_SPLIT_NUM_COUNTERS = 6
+};
+
+/* Floats of one rank's exchange row (the layout above); 0 on bad input. */
+int64_t cvsa_split_row_floats(const cvsa_split_desc_t* sd);
+
+/* This rank's part of exchange A from its page scores [batch, num_kv_heads,
+ * max_pages] (cvsa_score_pages) and local context lengths [batch]; the cached
+ * selection (rows of max_sel local pages, counts) may be NULL. Writes the
+ * exchange row and proposal_pages [rows, max_sel] (local page of each
+ * candidate slot, -1 unused). Candidates are pages outside the rank's forced
+ * pages with finite scores; the best are (score descending, page ascending). */
+int cvsa_split_propose(const cvsa_split_desc_t* sd, const float* page_scores,
+                       const int32_t* context_lens, const int32_t* cached_indices,
+                       const int32_t* cached_n, float* exchange_row, int32_t* proposal_pages,
+                       void* stream);
+
+/* After the all-gather of exchange rows (exchange [world, row_stride]): the
+ * global top-`budget` of the gathered candidates, the coverage gate of that
+ * selection (its candidates plus every rank's forced pages against the sum
+ * over all ranks' pages; coverage.py:160-215), the lazy gate of the cached
+ * selection when has_cache, and this rank's share of the new selection (its
+ * sink pages, its chosen pages, its local pages; ascending) in sel [rows,
+ * max_sel] / n_sel [rows] with its bitmap [rows, ceil(max_pages / 32)]
+ * (nullable); accept [rows] = the new selection's gate. Identical on every
+ * rank. state [4] int32, zeroed once and left zeroed except state[3], the
+ * decision word (bit0: every head accepted the cached selection, so the
+ * cached one is decoded; backend.py:446). stats_mode bit0: this is a lazy
+ * check step, bit1: lazy mode; counters [CVSA_SPLIT_NUM_COUNTERS] or NULL. */
+int cvsa_split_gate(const cvsa_split_desc_t* sd, const float* exchange, int64_t row_stride,
+                    const int32_t* proposal_pages, const int32_t* context_lens,
+                    int32_t has_cache, int32_t stats_mode, int32_t* sel, int32_t* n_sel,
+                    uint8_t* accept, uint32_t* bitmap, int32_t* state, int64_t* counters,
+                    int32_t* dev_error, void* stream);
+
+/* The attention of a page-split scoring / lazy-check step, into the partials
+ * of exchange B (o_unnorm [B, Hq, D], m, l [B, Hq] float32): heads decode the
+ * cached selection when decision (nullable) has bit0 set, else the new one
+ * (sel / n_sel), and a head whose new gate rejected (accept == 0) attends
+ * every valid page of the rank (exact recovery: draft and complement
+ * together, backend.py:818-844). When the new selection is decoded it is
+ * copied into cached_indices / cached_n (nullable: no copy). The workspace is
+ * cvsa_decode_workspace_size(qd, kv, max_sel) bytes. */
+int cvsa_split_attend(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
+                      int32_t* cached_indices, int32_t* cached_n, const int32_t* sel,
+                      const int32_t* n_sel, int32_t max_sel, const int32_t* decision,
+                      const uint8_t* accept, const uint32_t* bitmap, float* o_unnorm, float* m,
+                      float* l, int32_t* dev_error, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /* Fused exact recovery: for heads with accept == 0, attend to the valid pages
  * NOT in the selection (skipped through a selection bitmap, never
  * materialised as an index list) and LSE-merge that complement partial with

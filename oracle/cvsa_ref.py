@@ -870,3 +870,165 @@ class PagedKVRef:
         idx = torch.as_tensor(blocks, dtype=torch.long)
         return (self.k[idx].reshape(-1, *self.k.shape[2:]),
                 self.v[idx].reshape(-1, *self.v.shape[2:]))
+
+
+# --------------------------------------------------------------------------
+# page split over ranks (the scoring / lazy-check step of
+# cvsa/backend.py:683-864 and :392-465 with every sequence's pages spread over
+# ranks): restatement of the three per-rank ops of a split step
+# --------------------------------------------------------------------------
+
+def _lse_rows(x: torch.Tensor) -> torch.Tensor:
+    """log-sum-exp over the last dim (-inf when empty or all -inf)."""
+    if x.shape[-1] == 0:
+        return torch.full(x.shape[:-1], NEG_INF, dtype=torch.float32)
+    return torch.logsumexp(x.float(), -1)
+
+
+def split_propose(scores: torch.Tensor, context_lens: torch.Tensor, block_size: int,
+                  cached, sink: int, local: int, budget: int, max_sel: int,
+                  out: torch.Tensor) -> torch.Tensor:
+    """A rank's exchange row: [lse_all | lse_cached | lse_forced | candidate
+    scores] over its B * H rows (the candidates: the best `budget` of its
+    pages outside its forced ones, finite scores only, ranked (score desc,
+    page asc), written in page order and -inf padded to max_sel). Returns the
+    candidates' local pages [B, H, max_sel] (-1 unused)."""
+    B, H, W = scores.shape
+    rows = B * H
+    nv = n_valid_pages(context_lens, block_size).clamp(max=W)
+    lse_all = _lse_rows(scores).reshape(rows)
+    lse_c = torch.full((B, H), NEG_INF)
+    lse_f = torch.full((B, H), NEG_INF)
+    cand_s = torch.full((B, H, max_sel), NEG_INF)
+    prop = torch.full((B, H, max_sel), -1, dtype=torch.int32)
+    for b in range(B):
+        n = int(nv[b])
+        f_hi = min(sink, n)
+        t_lo = max(n - local, f_hi)
+        forced = list(range(f_hi)) + list(range(t_lo, n))
+        for h in range(H):
+            s = scores[b, h]
+            if forced:
+                lse_f[b, h] = _lse_rows(s[torch.tensor(forced)])
+            if cached is not None:
+                ci, cn = cached
+                ents = [int(p) for p in ci[b, h, :int(cn[b, h])] if 0 <= int(p) < W]
+                if ents:
+                    lse_c[b, h] = _lse_rows(s[torch.tensor(ents)])
+            sl = s.tolist()
+            cand = [p for p in range(f_hi, t_lo) if math.isfinite(sl[p])]
+            best = sorted(sorted(cand, key=lambda p: (-sl[p], p))[:budget])
+            for j, p in enumerate(best):
+                cand_s[b, h, j] = sl[p]
+                prop[b, h, j] = p
+    out[:rows] = lse_all
+    out[rows:2 * rows] = lse_c.reshape(rows)
+    out[2 * rows:3 * rows] = lse_f.reshape(rows)
+    out[3 * rows:3 * rows + rows * max_sel] = cand_s.reshape(-1)
+    return prop
+
+
+def split_gate(parts: torch.Tensor, prop: torch.Tensor, context_lens: torch.Tensor,
+               block_size: int, max_pages: int, rank: int, budget: int, max_sel: int,
+               sink: int, local: int, tau: float, has_cache: bool, stats_mode: int,
+               state: torch.Tensor, counters: torch.Tensor):
+    """The same decisions on every rank from the gathered rows parts [N, stride]:
+    lse_all over ranks, the lazy gate of the cached selection (batch decision
+    in state[3]), the global top-`budget` of the candidates (position order is
+    page order), its gate against lse_all with every rank's forced pages added,
+    and this rank's share of it (sink, chosen, local; ascending). Counts the
+    step in `counters` (scoring, accept, reject, heads accepted, checks, heads
+    total) the way cvsa/backend.py:420-465 (lazy) and :775-862 do. Returns
+    (sel, n, accept uint8, bitmap)."""
+    N = parts.shape[0]
+    B, H, _ = prop.shape
+    rows = B * H
+    lse_all = torch.logsumexp(parts[:, :rows].float(), 0)
+    lse_c = torch.logsumexp(parts[:, rows:2 * rows].float(), 0)
+    forced = parts[:, 2 * rows:3 * rows].float()                       # [N, rows]
+    cand = parts[:, 3 * rows:3 * rows + rows * max_sel].reshape(N, rows, max_sel)
+    cand = cand.permute(1, 0, 2).reshape(rows, N * max_sel)
+    acc0 = torch.exp(lse_c - lse_all) >= tau
+    nv = n_valid_pages(context_lens, block_size).clamp(max=max_pages)
+    sel = torch.zeros((B, H, max_sel), dtype=torch.int32)
+    n = torch.zeros((B, H), dtype=torch.int32)
+    acc = torch.zeros((B, H), dtype=torch.uint8)
+    words = (max_pages + 31) // 32
+    bitmap = torch.zeros((B, H, words), dtype=torch.int64)
+    for i in range(rows):
+        b, h = divmod(i, H)
+        c = cand[i].tolist()
+        fin = [j for j in range(len(c)) if math.isfinite(c[j])]
+        chosen = sorted(fin, key=lambda j: (-c[j], j))[:budget]
+        terms = torch.tensor([c[j] for j in chosen] + forced[:, i].tolist())
+        lse_sel = _lse_rows(terms)
+        acc[b, h] = int(bool(torch.exp(lse_sel - lse_all[i]) >= tau))
+        mine = sorted(j - rank * max_sel for j in chosen
+                      if rank * max_sel <= j < (rank + 1) * max_sel)
+        nvb = int(nv[b])
+        f_hi = min(sink, nvb)
+        t_lo = max(nvb - local, f_hi)
+        pages = list(range(f_hi)) + [int(prop[b, h, j]) for j in mine] + list(range(t_lo, nvb))
+        n[b, h] = len(pages)
+        if pages:
+            sel[b, h, :len(pages)] = torch.tensor(pages, dtype=torch.int32)
+        for p in pages:
+            bitmap[b, h, p // 32] |= 1 << (p % 32)
+    reuse = bool(has_cache) and bool(acc0.all())
+    state[3] = 1 if reuse else 0
+    check, lazy = bool(stats_mode & 1), bool(stats_mode & 2)
+    SC, AC, RJ, HA, CK, HT = range(6)
+    if check:
+        counters[CK] += 1
+    if check and not has_cache:
+        counters[RJ] += 1
+    if check and has_cache:
+        counters[HT] += rows
+        counters[HA] += int(acc0.sum())
+        counters[AC if reuse else RJ] += 1
+        if not reuse:
+            counters[SC] += 1
+    else:
+        counters[SC] += 1
+    if not lazy:
+        counters[HA] += int(acc.sum())
+        counters[HT] += rows
+    bitmap = torch.where(bitmap >= 2 ** 31, bitmap - 2 ** 32, bitmap).to(torch.int32)
+    return sel, n, acc, bitmap
+
+
+def split_attend(q, k_cache, v_cache, block_tables, context_lens, num_kv_heads, num_q_per_kv,
+                 block_size, cached, sel, n, decision, accept, bitmap, out):
+    """Partials of a split step: the cached selection where decision[0] bit0
+    is set, else the new one; a head whose new gate rejected attends every
+    valid page of the rank (draft and complement of backend.py:818-844).
+    Copies the new selection into `cached` when it is the one decoded."""
+    B = q.shape[0]
+    H = num_kv_heads
+    W = block_tables.shape[1]
+    reuse = decision is not None and (int(decision[0]) & 1) == 1
+    if reuse:
+        idx, cnt = cached[0].clone(), cached[1].clone()
+    else:
+        nv = n_valid_pages(context_lens, block_size).clamp(max=W)
+        every = torch.arange(W, dtype=torch.int32).view(1, 1, W).expand(B, H, W)
+        width = max(W, sel.shape[-1])
+        idx = torch.zeros((B, H, width), dtype=torch.int32)
+        cnt = torch.zeros((B, H), dtype=torch.int32)
+        for b in range(B):
+            for h in range(H):
+                if int(accept[b, h]):
+                    k = int(n[b, h])
+                    idx[b, h, :k] = sel[b, h, :k]
+                    cnt[b, h] = k
+                else:
+                    idx[b, h, :W] = every[b, h]
+                    cnt[b, h] = int(nv[b])
+        if cached is not None:
+            cached[0].copy_(sel)
+            cached[1].copy_(n)
+    o, m, l = sparse_decode_unnorm(q, k_cache, v_cache, block_tables, idx, cnt, context_lens,
+                                   num_kv_heads, num_q_per_kv, block_size)
+    for dst, src in zip(out, (o, m, l)):
+        dst.copy_(src)
+    return out

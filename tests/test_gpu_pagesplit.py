@@ -146,3 +146,82 @@ def test_page_split_steps_replay_as_graphs(cuda):
                     union += [p + int(lo[b]) for p in li[b, h, :int(ln[b, h])].tolist()]
                 assert union == fi[b, h, :int(fn[b, h])].tolist(), (step, b, h)
         full.step_done(0, 1)
+
+
+def _rank_scores(gen, B, H, W, lens, ties):
+    """Page scores of one rank: -inf past each sequence's valid pages, some
+    exact ties (ties=True), one non-finite valid page."""
+    s = torch.randn((B, H, W), generator=gen)
+    if ties:
+        s = (s * 4).round() / 4           # many equal values
+    nv = (lens.long() + 15) // 16
+    for b in range(B):
+        s[b, :, int(nv[b]):] = float("-inf")
+        if int(nv[b]) > 3:
+            s[b, 0, 2] = float("-inf")      # a valid page with a -inf score
+    return s
+
+
+@pytest.mark.parametrize("world,ties", [(3, True), (2, False), (4, True)])
+def test_split_kernels_match_oracle(cuda, world, ties):
+    """cvsa_split_propose / cvsa_split_gate against their oracle restatement
+    on the same inputs: exchange rows (log-sum-exps within 1e-5, candidates and
+    their pages exactly), then from the same gathered rows every rank's
+    selection, bitmap, gate, decision word and counters exactly (gates away
+    from the threshold). Ragged ranks, one with fewer candidates than the
+    budget, forced sink / local pages, ties and a -inf page."""
+    from cvsa.kernels import split as SK
+    gen = torch.Generator().manual_seed(100 + world)
+    B, H, budget, sink, local = 3, 4, 7, 1, 2
+    max_sel = budget + sink + local
+    lens_all = torch.tensor([[700, 100, 2000], [650, 40, 1900], [600, 90, 1800],
+                             [640, 60, 1700]], dtype=torch.int32)[:world]
+    W = int(((lens_all.long() + 15) // 16).max())
+    rows_dev, props, inputs = [], [], []
+    for r in range(world):
+        lens = lens_all[r]
+        s = _rank_scores(gen, B, H, W, lens, ties)
+        sink_r = sink if r == 0 else 0
+        local_r = local if r == world - 1 else 0
+        ci = torch.randint(0, W, (B, H, max_sel), generator=gen, dtype=torch.int32)
+        cn = torch.randint(0, max_sel + 1, (B, H), generator=gen, dtype=torch.int32)
+        n_row = SK.row_floats(B, H, max_sel)
+        row_d = torch.empty(n_row, dtype=torch.float32, device=cuda)
+        prop_d = SK.split_propose(s.to(cuda), lens.to(cuda), 16, (ci.to(cuda), cn.to(cuda)),
+                                  sink_r, local_r, budget, max_sel, row_d)
+        row_o = torch.empty(n_row, dtype=torch.float32)
+        prop_o = R.split_propose(s, lens, 16, (ci, cn), sink_r, local_r, budget, max_sel, row_o)
+        rd = row_d.cpu()
+        rows = B * H
+        assert torch.allclose(rd[:3 * rows], row_o[:3 * rows], atol=1e-5, rtol=1e-5,
+                              equal_nan=False), r
+        assert torch.equal(rd[3 * rows:], row_o[3 * rows:]), r
+        assert torch.equal(prop_d.cpu(), prop_o), r
+        rows_dev.append(rd)
+        props.append((prop_d, prop_o))
+        inputs.append((lens, sink_r, local_r))
+    parts = torch.stack(rows_dev)
+    tau = 0.6
+    for r in range(world):
+        lens, sink_r, local_r = inputs[r]
+        state_d = torch.zeros(4, dtype=torch.int32, device=cuda)
+        ctr_d = torch.zeros(6, dtype=torch.int64, device=cuda)
+        state_o = torch.zeros(4, dtype=torch.int32)
+        ctr_o = torch.zeros(6, dtype=torch.int64)
+        for has_cache, mode in ((True, 3), (False, 3), (False, 0)):
+            got_d = SK.split_gate(parts.to(cuda), props[r][0], lens.to(cuda), 16, W, r, budget,
+                                  max_sel, sink_r, local_r, tau, has_cache, mode, state_d, ctr_d)
+            got_o = R.split_gate(parts, props[r][1], lens, 16, W, r, budget, max_sel, sink_r,
+                                 local_r, tau, has_cache, mode, state_o, ctr_o)
+            sel_d, n_d, acc_d, bm_d = (t.cpu() for t in got_d)
+            sel_o, n_o, acc_o, bm_o = got_o
+            assert torch.equal(n_d, n_o), (r, has_cache)
+            for b in range(B):
+                for h in range(H):
+                    k = int(n_o[b, h])
+                    assert sel_d[b, h, :k].tolist() == sel_o[b, h, :k].tolist(), (r, b, h)
+            assert torch.equal(bm_d, bm_o), r
+            assert torch.equal(acc_d, acc_o), r
+            assert int(state_d[3]) == int(state_o[3]), r
+            assert torch.equal(state_d[:3].cpu(), torch.zeros(3, dtype=torch.int32)), r
+        assert torch.equal(ctr_d.cpu(), ctr_o), r

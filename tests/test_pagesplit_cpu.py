@@ -2,8 +2,9 @@
 
 Each rank holds a contiguous range of every sequence's pages
 (pagesplit.shard_sequence) and runs PageSplitBackend with the oracle's
-scoring, selection and decode in place of the CUDA kernels, exchanging
-proposals and partials over a real gloo group. Every rank's output must
+scoring, split proposal / gate / attention and merge in place of the CUDA
+kernels, exchanging the proposal rows and the partials over a real gloo
+group. Every rank's output must
 equal the oracle backend's over the whole context (the single-GPU
 semantics), its cached selection must be the oracle's selection restricted
 to its pages, and every rank must take the same reuse / rescore decisions.
@@ -28,13 +29,9 @@ from oracle import cvsa_ref as R
 class OracleOps:
     """The oracle's restatement of the kernels a page-split step runs."""
     score_pages = staticmethod(R.score_pages)
-
-    @staticmethod
-    def select_pages(scores, cl, bs, budget, sink, local, max_sel=None):
-        idx, n = R.select_pages(scores, cl, bs, budget, sink, local)
-        if max_sel is not None and idx.shape[-1] < max_sel:
-            idx = torch.nn.functional.pad(idx, (0, max_sel - idx.shape[-1]))
-        return idx, n
+    split_propose = staticmethod(R.split_propose)
+    split_gate = staticmethod(R.split_gate)
+    split_attend = staticmethod(R.split_attend)
 
     @staticmethod
     def decode_unnorm(q, k, v, bt, idx, n, cl, H, G, bs, out=None):
@@ -44,22 +41,6 @@ class OracleOps:
         for dst, src in zip(out, (o, m, l)):
             dst.copy_(src)
         return out
-
-    @staticmethod
-    def page_lse(scores, idx, n):
-        """log-sum-exp over every page and over the first n selected pages
-        (the two sums of coverage.py:179-215)."""
-        K = idx.shape[-1]
-        mask = torch.arange(K).view(1, 1, K) < n.unsqueeze(-1)
-        sel = torch.gather(scores, -1, idx.long().clamp(min=0)).masked_fill(~mask,
-                                                                             float("-inf"))
-        return torch.logsumexp(scores, -1), torch.logsumexp(sel, -1)
-
-    @staticmethod
-    def rank_accept(parts, off_all, off_sel, rows, tau):
-        lse_all = torch.logsumexp(parts[:, off_all:off_all + rows], 0)
-        lse_sel = torch.logsumexp(parts[:, off_sel:off_sel + rows], 0)
-        return torch.exp(lse_sel - lse_all) >= tau
 
     @staticmethod
     def rank_merge(parts, B, H, G, D, out, need=None):
