@@ -373,9 +373,9 @@ C4_POOLS = 16
 def measure_config4(dev, steps, warmup, ws, rank):
     """Config 4 (Llama-70B attention: B=8, Hq=64, Hkv=8, D=128, ctx 32768, 80
     layers), KV heads sharded over the ranks: rank r holds KV heads
-    [8r/N, 8(r+1)/N) and their query heads, and the lazy check step all-reduces
-    the batch-global decision (one int32, MIN, NCCL) between its selection and
-    attention halves. Layer l reads pool l % C4_POOLS (each pool 1.07 GB / N of
+    [8r/N, 8(r+1)/N) and their query heads, and the lazy check step reduces
+    the batch-global decision (one int32, MIN, an NVLink peer-memory kernel)
+    between its selection and attention halves. Layer l reads pool l % C4_POOLS (each pool 1.07 GB / N of
     K+V, so consecutive uses of a pool are 15 pools apart, far beyond L2). The
     lazy-check and reuse steps are captured as CUDA graphs (the all-reduce
     inside) and timed separately; times are the max over ranks."""
@@ -392,9 +392,13 @@ def measure_config4(dev, steps, warmup, ws, rank):
     if ws > 1:
         import torch.distributed as dist
         pg = dist.group.WORLD
+    px = None
+    if ws > 1:
+        from cvsa.peer import PeerExchange
+        px = PeerExchange(4, group=pg, device=dev)
     be = CVSABackend(hkv, Hq, D, 16, num_layers=C4_LAYERS, budget_pct=0.05,
                      coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
-                     sink_pages=1, local_pages=2, process_group=pg)
+                     sink_pages=1, local_pages=2, process_group=pg, peer_exchange=px)
 
     def step():
         for l in range(C4_LAYERS):
@@ -404,7 +408,8 @@ def measure_config4(dev, steps, warmup, ws, rank):
 
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
-    graphs, launch = {}, "CUDA graph per step kind (NCCL all-reduce inside the lazy-check graph)"
+    graphs, launch = {}, ("CUDA graph per step kind (the decision's NVLink peer-memory MIN "
+                          "kernel inside the lazy-check graph)")
     with torch.cuda.stream(side):
         for _ in range(max(warmup, M_INTERVAL)):
             step()
@@ -468,6 +473,11 @@ def measure_config4(dev, steps, warmup, ws, rank):
         res[kind] = (ms * 1e3 / (n * C4_LAYERS), _sum_over_ranks(per_rank_bytes, ws) / (ms * 1e-3) / 1e9)
     stats = be.get_stats()
     del graphs
+    if px is not None:
+        torch.cuda.synchronize()
+        if int(px.dev_error.item()):
+            launch += "; peer exchange reported a timeout"
+        px.close()
     us_layer = (res["lazy"][0] + (M_INTERVAL - 1) * res["reuse"][0]) / M_INTERVAL
     step_s = us_layer * C4_LAYERS * 1e-6
     gbs = (res["lazy"][1] * res["lazy"][0] + (M_INTERVAL - 1) * res["reuse"][1] * res["reuse"][0]) / (
@@ -487,7 +497,7 @@ def measure_config4(dev, steps, warmup, ws, rank):
 C3S_LAYERS = 4
 
 
-def measure_config3_split(dev, steps, ws, rank):
+def measure_config3_split(dev, steps, ws, rank, peer=False):
     """Config 3 (one 128K sequence) with its pages split over the ranks
     (cvsa.pagesplit): every rank scores, proposes and attends its contiguous
     page range; the proposal rows (candidates and coverage sums) and the
@@ -511,9 +521,17 @@ def measure_config3_split(dev, steps, ws, rank):
     if ws > 1:
         import torch.distributed as dist
         pg = dist.group.WORLD
+    px = None
+    if peer and ws > 1:
+        from cvsa.kernels.select import budget_for
+        from cvsa.peer import PeerExchange
+        W = pools[0][6]
+        max_sel = budget_for(int(W), 0.05) + 3
+        px = PeerExchange(PageSplitBackend.exchange_row_cap(1, 8, 32, 128, max_sel), group=pg,
+                          device=dev)
     pb = PageSplitBackend(8, 32, 128, 16, rank, ws, num_layers=C3S_LAYERS, budget_pct=0.05,
                           coverage_threshold=0.9, lazy=True, check_interval=M_INTERVAL,
-                          sink_pages=1, local_pages=2, process_group=pg)
+                          sink_pages=1, local_pages=2, process_group=pg, exchange=px)
     if ws > 1:
         ag = dist_allgather(pg)
     else:
@@ -580,12 +598,20 @@ def measure_config3_split(dev, steps, ws, rank):
     del graphs
     us_layer = (res["check"] + (M_INTERVAL - 1) * res["reuse"]) / M_INTERVAL
     breakdown = _split_breakdown(pb, pools, ag, ws)
+    errors = 0
+    if px is not None:
+        torch.cuda.synchronize()
+        errors = int(px.dev_error.item())
+        px.close()
+    xname = "NVLink peer-memory kernels (all-gather; push + merge)" if px is not None else \
+        "NCCL all-gathers"
     return {"workload": "config3: B=1, Hq=32, Hkv=8, D=128, bf16, ctx=131072 (8192 pages), "
                         f"pages split contiguously over {ws} GPU(s), lazy M=4, {C3S_LAYERS} layers",
             "us_per_layer_lazy_check": res["check"], "us_per_layer_reuse": res["reuse"],
             "us_per_layer": us_layer, "steps_per_kind": n,
-            "launch": ("CUDA graph per step kind (NCCL all-gathers inside)" if ok else
-                       "eager (graph capture of the collectives failed)"),
+            "exchange": xname, "exchange_errors": errors,
+            "launch": (f"CUDA graph per step kind ({xname} inside)" if ok else
+                       "eager (graph capture failed)"),
             "breakdown_us_per_layer": breakdown,
             "stats_rank0_warmup": stats}
 
@@ -617,14 +643,23 @@ def _split_breakdown(pb, pools, ag, ws):
     ops = pb.ops
     pb.ops = types.SimpleNamespace(**{nm: wrap(nm, getattr(ops, nm)) for nm in names})
     tag = wrap("all_gather", ag)
+    px = pb.exchange
+    if px is not None:
+        pb.exchange = types.SimpleNamespace(allgather=wrap("all_gather", px.allgather),
+                                            merge=wrap("exchange_merge", px.merge))
     out = {}
     try:
         for kind, step_idx in (("check", 0), ("reuse", 1)):
             records.clear()
             pb._step = step_idx
             # hold the stream (a fixed spin of about 25 ms) while the host
-            # enqueues the step, so no event pair spans host launch gaps
+            # enqueues the step, so no event pair spans host launch gaps, and
+            # let the ranks meet on the device after it, so no exchange
+            # absorbs the ranks' start skew
             torch.cuda._sleep(50_000_000)
+            if ws > 1:
+                import torch.distributed as dist
+                dist.all_reduce(torch.zeros(1, device="cuda"))
             for l, (q, k, v, bt, cl, ctx, W) in enumerate(pools):
                 run_step(pb.step(q, k, v, bt, cl, l, ctx, W), tag)
             torch.cuda.synchronize()
@@ -633,9 +668,11 @@ def _split_breakdown(pb, pools, ag, ws):
                 tot[label] = tot.get(label, 0.0) + e0.elapsed_time(e1)
             out[kind] = {label: _max_over_ranks(tot.get(label, 0.0), ws) * 1e3 / len(pools)
                          for label in ("score_pages", "split_propose", "all_gather", "split_gate",
-                                       "split_attend", "decode_unnorm", "rank_merge")}
+                                       "split_attend", "decode_unnorm", "rank_merge",
+                                       "exchange_merge")}
     finally:
         pb.ops = ops
+        pb.exchange = px
     return out
 
 
@@ -1001,7 +1038,11 @@ def run_cvsa(args, ws, rank, local):
         c5 = measure_config5(dev, warm, ws, rank)
     c3s = None
     if not args.no_c3:
-        c3s = measure_config3_split(dev, args.steps, ws, rank)
+        c3s = measure_config3_split(dev, args.steps, ws, rank, peer=ws > 1)
+        if ws > 1:
+            nccl = measure_config3_split(dev, args.steps, ws, rank, peer=False)
+            c3s["nccl_all_gathers"] = {k: nccl[k] for k in (
+                "us_per_layer_lazy_check", "us_per_layer_reuse", "us_per_layer")}
 
     # ---- CPU baseline (rank 0, N=1 only) ----
     cpu = None

@@ -3,7 +3,8 @@
 // This layer validates arguments (returning the status codes the Python
 // shims map to the reference's exceptions), carves caller-provided
 // workspaces, and sequences the kernels of one CVSA layer step on the
-// caller's stream. It never allocates device memory and never synchronises.
+// caller's stream. It never synchronises, and allocates device memory only in
+// the set-up call cvsa_peer_alloc.
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -567,6 +568,107 @@ int cvsa_split_attend(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,
   p.head_done = ws_head_done(workspace);
   return cuda_status(launch_attend(q, kv, p, max_sel, (cudaStream_t)stream, false),
                      "split attend launch");
+}
+
+namespace {
+int check_peer(const cvsa_peer_desc_t* pd, PeerView* pv) {
+  if (!pd) return fail(CVSA_ERR_INVALID, "NULL peer descriptor");
+  pv->bases = pd->bases;
+  pv->world = pd->world;
+  pv->rank = pd->rank;
+  pv->row_cap = pd->row_cap;
+  pv->dev_err = pd->dev_error;
+  if (!peer_shape_ok(*pv)) return fail(CVSA_ERR_INVALID, "bad peer descriptor (world <= 8)");
+  return CVSA_OK;
+}
+}  // namespace
+
+size_t cvsa_peer_buffer_bytes(int32_t world, int64_t row_cap) {
+  if (world < 1 || world > 8 || row_cap <= 0) return 0;
+  return peer_buffer_bytes(world, row_cap);
+}
+
+int cvsa_peer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
+  if (!ptr || !ipc_handle || bytes == 0) return fail(CVSA_ERR_INVALID, "bad peer_alloc arguments");
+  void* p = nullptr;
+  int st = cuda_status(cudaMalloc(&p, bytes), "cudaMalloc (peer buffer)");
+  if (st) return st;
+  st = cuda_status(cudaMemset(p, 0, bytes), "cudaMemset (peer buffer)");
+  if (!st) {
+    cudaIpcMemHandle_t h;
+    st = cuda_status(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+    if (!st) memcpy(ipc_handle, &h, sizeof(h));
+  }
+  if (st) {
+    cudaFree(p);
+    return st;
+  }
+  *ptr = p;
+  return CVSA_OK;
+}
+
+int cvsa_peer_open(const void* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess),
+                     "cudaIpcOpenMemHandle");
+}
+
+int cvsa_peer_close(void* ptr) {
+  if (!ptr) return CVSA_OK;
+  return cuda_status(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+}
+
+int cvsa_peer_free(void* ptr) {
+  if (!ptr) return CVSA_OK;
+  return cuda_status(cudaFree(ptr), "cudaFree (peer buffer)");
+}
+
+int cvsa_peer_allgather(const cvsa_peer_desc_t* pd, const float* src, int64_t n, float* out,
+                        void* stream) {
+  PeerView pv;
+  int st = check_peer(pd, &pv);
+  if (st) return st;
+  if (n < 0 || n > pv.row_cap) return fail(CVSA_ERR_INVALID, "n outside [0, row_cap]");
+  if (n == 0) return CVSA_OK;
+  if (!src || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  if (n > (int64_t)peer_max_ctas() * 1024) return fail(CVSA_ERR_UNSUPPORTED, "row too long");
+  return cuda_status(launch_peer_gather(pv, src, n, out, false, (cudaStream_t)stream),
+                     "peer allgather launch");
+}
+
+int cvsa_peer_min_i32(const cvsa_peer_desc_t* pd, const int32_t* src, int64_t n, int32_t* out,
+                      void* stream) {
+  PeerView pv;
+  int st = check_peer(pd, &pv);
+  if (st) return st;
+  if (n < 0 || n > pv.row_cap) return fail(CVSA_ERR_INVALID, "n outside [0, row_cap]");
+  if (n == 0) return CVSA_OK;
+  if (!src || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  if (n > (int64_t)peer_max_ctas() * 1024) return fail(CVSA_ERR_UNSUPPORTED, "row too long");
+  return cuda_status(launch_peer_gather(pv, reinterpret_cast<const float*>(src), n,
+                                        reinterpret_cast<float*>(out), true, (cudaStream_t)stream),
+                     "peer min launch");
+}
+
+int cvsa_peer_merge(const cvsa_peer_desc_t* pd, const float* part, int32_t batch,
+                    int32_t num_kv_heads, int32_t num_q_per_kv, int32_t head_dim,
+                    const uint8_t* need, void* out, int32_t out_dtype, void* stream) {
+  PeerView pv;
+  int st = check_peer(pd, &pv);
+  if (st) return st;
+  if (batch < 0 || num_kv_heads <= 0 || num_q_per_kv <= 0 || head_dim <= 0)
+    return fail(CVSA_ERR_INVALID, "bad shape");
+  if (!valid_dtype(out_dtype)) return fail(CVSA_ERR_INVALID, "out dtype unknown");
+  const int64_t rows = (int64_t)batch * num_kv_heads * num_q_per_kv;
+  if (rows * (head_dim + 2) > pv.row_cap) return fail(CVSA_ERR_INVALID, "row_cap too small");
+  if (rows == 0) return CVSA_OK;
+  if (!part || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
+  if ((rows + 3) / 4 > peer_max_ctas()) return fail(CVSA_ERR_UNSUPPORTED, "too many query rows");
+  return cuda_status(launch_peer_merge(pv, part, batch, num_kv_heads, num_q_per_kv, head_dim,
+                                       need, out, out_dtype, (cudaStream_t)stream),
+                     "peer merge launch");
 }
 
 int cvsa_recover_merge(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kvd,

@@ -209,6 +209,21 @@ size_t split_gate_smem(int world, int max_sel, int bitmap_words);
 cudaError_t launch_split_propose(const SplitProposeParams& p, cudaStream_t s, bool pdl);
 cudaError_t launch_split_gate(const SplitGateParams& p, cudaStream_t s, bool pdl);
 
+// ---- peer.cu (exchanges over NVLink peer memory) ----
+struct PeerView {
+  const uint64_t* bases;  // [world] device array: every rank's exchange buffer mapped here
+  int world, rank;
+  int64_t row_cap;        // floats per rank row
+  int32_t* dev_err;
+};
+size_t peer_buffer_bytes(int world, int64_t row_cap);
+bool peer_shape_ok(const PeerView& pv);
+int peer_max_ctas();
+cudaError_t launch_peer_gather(const PeerView& pv, const float* src, int64_t n, float* out,
+                               bool min_i32, cudaStream_t s);
+cudaError_t launch_peer_merge(const PeerView& pv, const float* part, int B, int hkv, int G, int D,
+                              const uint8_t* need, void* out, int out_dtype, cudaStream_t s);
+
 // ---- merge.cu ----
 cudaError_t launch_lse_merge(const float* o_d, const float* m_d, const float* l_d,
                              const float* o_c, const float* m_c, const float* l_c,

@@ -87,6 +87,13 @@ class SplitDesc(ctypes.Structure):
     ]
 
 
+class PeerDesc(ctypes.Structure):
+    _fields_ = [
+        ("bases", ctypes.c_void_p), ("world", ctypes.c_int32), ("rank", ctypes.c_int32),
+        ("row_cap", ctypes.c_int64), ("dev_error", ctypes.c_void_p),
+    ]
+
+
 _P = ctypes.c_void_p
 _I = ctypes.c_int32
 _SIGS = {
@@ -113,6 +120,15 @@ _SIGS = {
                          _P, _P, _P, _P, _P, _P], ctypes.c_int),
     "cvsa_split_attend": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _P, _P, _P, _I,
                            _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P], ctypes.c_int),
+    "cvsa_peer_buffer_bytes": ([_I, ctypes.c_int64], ctypes.c_size_t),
+    "cvsa_peer_alloc": ([ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), _P], ctypes.c_int),
+    "cvsa_peer_open": ([_P, ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "cvsa_peer_close": ([_P], ctypes.c_int),
+    "cvsa_peer_free": ([_P], ctypes.c_int),
+    "cvsa_peer_allgather": ([ctypes.POINTER(PeerDesc), _P, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "cvsa_peer_min_i32": ([ctypes.POINTER(PeerDesc), _P, ctypes.c_int64, _P, _P], ctypes.c_int),
+    "cvsa_peer_merge": ([ctypes.POINTER(PeerDesc), _P, _I, _I, _I, _I, _P, _P, _I, _P],
+                        ctypes.c_int),
     "cvsa_rank_merge": ([_P, _I, ctypes.c_int64, _I, _I, _I, _I, _P, _P, _I, _P], ctypes.c_int),
     "cvsa_recover_merge": ([ctypes.POINTER(QueryDesc), ctypes.POINTER(KvDesc), _P, _I, _P, _P, _P,
                             _P, _P, _P, _I, _P, ctypes.c_size_t, _P], ctypes.c_int),

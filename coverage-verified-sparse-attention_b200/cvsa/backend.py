@@ -119,6 +119,7 @@ class CVSABackend:
         local_pages: int = 0,
         keep_page_scores: bool = False,
         process_group=None,
+        peer_exchange=None,
     ):
         # argument checks of the reference (backend.py:150-178)
         if selector not in ("exact", "quest"):
@@ -169,6 +170,9 @@ class CVSABackend:
         self.local_pages = local_pages
         self.keep_page_scores = keep_page_scores
         self.process_group = process_group
+        # a cvsa.peer.PeerExchange over the same ranks: the decision word is
+        # reduced by an NVLink peer-memory kernel instead of dist.all_reduce
+        self.peer_exchange = peer_exchange
         self._decision_views: Dict[int, torch.Tensor] = {}  # workspace ptr -> int32 view
 
         self._layers: Dict[int, _LayerState] = {}
@@ -331,7 +335,7 @@ class CVSABackend:
         h = self.begin_step(q, k_cache, v_cache, block_tables, context_lens, layer_idx,
                             phased=self.process_group is not None)
         if h.decision is not None:
-            exchange_decision(h.decision, self.process_group)
+            exchange_decision(h.decision, self.process_group, self.peer_exchange)
             self.finish_step(h)
         return h.out
 
@@ -524,11 +528,15 @@ class CVSABackend:
         return None if st is None else st.flags
 
 
-def exchange_decision(decision: torch.Tensor, group) -> torch.Tensor:
+def exchange_decision(decision: torch.Tensor, group, peer=None) -> torch.Tensor:
     """All-reduce the lazy decision word over `group` (MIN: bit0 stays set only
     if every rank's heads all accepted their cached selection), in place, in
     stream order. backend.py:446 takes `accept_mask.all()` over every head of
-    the batch; with the heads sharded over ranks that is this reduction."""
+    the batch; with the heads sharded over ranks that is this reduction. With
+    `peer` (a cvsa.peer.PeerExchange over the same ranks) it is one NVLink
+    peer-memory kernel (cvsa_peer_min_i32)."""
+    if peer is not None:
+        return peer.min_i32(decision)
     import torch.distributed as dist
     dist.all_reduce(decision, op=dist.ReduceOp.MIN, group=group)
     return decision

@@ -34,7 +34,10 @@ issues the same collectives.
 
 A step is a generator that yields each 1-D float32 tensor to all-gather and
 receives the [world, n] result; `run_step` drives it with torch.distributed,
-and tests can drive the ranks of one process in lockstep.
+and tests can drive the ranks of one process in lockstep. With an `exchange`
+(cvsa.peer.PeerExchange) the step yields nothing: exchange A is an all-gather
+kernel over NVLink peer memory and exchange B one kernel that pushes the
+partials and merges them.
 """
 
 from typing import Callable, Dict, Optional, Tuple
@@ -137,7 +140,7 @@ class PageSplitBackend:
                  rank: int, world: int, num_layers: int = 32, budget_pct: float = 0.10,
                  reuse_interval: int = 16, coverage_threshold: float = 0.90, lazy: bool = False,
                  check_interval: Optional[int] = None, sink_pages: int = 0, local_pages: int = 0,
-                 process_group=None, ops=None):
+                 process_group=None, ops=None, exchange=None):
         self.num_kv_heads = num_kv_heads
         self.num_q_heads = num_q_heads
         self.G = num_q_heads // num_kv_heads
@@ -153,6 +156,9 @@ class PageSplitBackend:
         self.sink_pages, self.local_pages = sink_pages, local_pages
         self.process_group = process_group
         self.ops = ops or DeviceOps()
+        # a cvsa.peer.PeerExchange: the two exchanges and the merge run as
+        # NVLink peer-memory kernels instead of yielding to an all-gather
+        self.exchange = exchange
         self._cached: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
         self._step = 0
         self._ctr: Optional[torch.Tensor] = None
@@ -180,6 +186,14 @@ class PageSplitBackend:
         gen = self.step(q, k_cache, v_cache, block_tables, context_lens, layer_idx,
                         global_context_lens, global_table_width)
         return run_step(gen, dist_allgather(self.process_group))
+
+    @staticmethod
+    def exchange_row_cap(batch: int, num_kv_heads: int, num_q_heads: int, head_dim: int,
+                         max_sel: int) -> int:
+        """Floats a PeerExchange for this backend must carry per rank: the
+        larger of the proposal row and the partial row."""
+        rows = batch * num_kv_heads
+        return max(3 * rows + rows * max_sel, batch * num_q_heads * (head_dim + 2))
 
     def _counters(self, dev) -> torch.Tensor:
         if self._ctr is None:
@@ -225,6 +239,8 @@ class PageSplitBackend:
         if not scoring and not check:                           # reuse step
             self.ops.decode_unnorm(q, k, v, bt, cached[0], cached[1], cl, H, G, bs,
                                    out=(o, m, l))
+            if self.exchange is not None:
+                return self.exchange.merge(buf, B, H, G, D, out)
             got = yield buf
             return self.ops.rank_merge(got, B, H, G, D, out)
 
@@ -241,7 +257,10 @@ class PageSplitBackend:
         row = torch.empty(3 * B * H + B * H * max_sel, dtype=torch.float32, device=dev)
         prop = self.ops.split_propose(scores, cl, bs, cached if has_cache else None, sink_r,
                                       local_r, budget, max_sel, row)
-        got = yield row                                         # exchange A
+        if self.exchange is not None:
+            got = self.exchange.allgather(row)                  # exchange A
+        else:
+            got = yield row                                     # exchange A
         state = self._state(dev)
         sel, n, acc, bitmap = self.ops.split_gate(got, prop, cl, bs, W_r, r, budget, max_sel,
                                                   sink_r, local_r, self.tau, has_cache,
@@ -254,5 +273,7 @@ class PageSplitBackend:
         # a captured reuse step keeps reading the same cache buffers
         self.ops.split_attend(q, k, v, bt, cl, H, G, bs, cached, sel, n,
                               state[3:4] if has_cache else None, acc, bitmap, out=(o, m, l))
+        if self.exchange is not None:
+            return self.exchange.merge(buf, B, H, G, D, out)   # exchange B and merge
         got = yield buf                                         # exchange B
         return self.ops.rank_merge(got, B, H, G, D, out)

@@ -11,7 +11,8 @@
  *   - All tensor pointers are DEVICE pointers on the current CUDA device.
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default
  *     stream). Every call only enqueues work on that stream; nothing blocks
- *     the host and nothing allocates memory: scratch comes from a
+ *     the host and nothing allocates memory (except the set-up call
+ *     cvsa_peer_alloc): scratch comes from a
  *     caller-provided workspace whose size is queried with *_workspace_size.
  *     A workspace is 256-byte aligned and zeroed once before its first use
  *     (cvsa_workspace_reset). Its first 256 KiB hold counters the kernels
@@ -63,7 +64,7 @@ enum {
   CVSA_DEV_ERR_PAGE_RANGE = 2,  /* a page index outside [0, max_pages) */
   CVSA_DEV_ERR_POOL = 4,        /* append: free list exhausted */
   CVSA_DEV_ERR_TABLE_FULL = 8,  /* append: sequence longer than the table */
-  CVSA_DEV_ERR_TIMEOUT = 16     /* a bounded wait on an async copy gave up */
+  CVSA_DEV_ERR_TIMEOUT = 16     /* a bounded wait (async copy, peer rank) gave up */
 };
 
 /* Paged KV pool: [num_blocks, block_size, num_kv_heads, head_dim].
@@ -307,6 +308,50 @@ int cvsa_split_attend(const cvsa_query_desc_t* qd, const cvsa_kv_desc_t* kv,
                       const uint8_t* accept, const uint32_t* bitmap, float* o_unnorm, float* m,
                       float* l, int32_t* dev_error, void* workspace, size_t workspace_bytes,
                       void* stream);
+
+/* ---- exchanges over NVLink peer memory (one process per GPU) -------------
+ * A replacement for the small all-gathers of the page split and the decision
+ * all-reduce of the head-sharded step: every rank allocates one exchange
+ * buffer (cvsa_peer_alloc), passes its 64-byte IPC handle to the other ranks
+ * (any host channel), maps theirs (cvsa_peer_open) and puts the world base
+ * pointers, in rank order, in a device array. A call stores this rank's row
+ * into every rank's buffer over NVLink, each 4-byte word beside the call's
+ * number in one 8-byte store, and reads the other ranks' words as they land
+ * (bounded waits: cvsa_set_wait_limit; CVSA_DEV_ERR_TIMEOUT when a rank never
+ * arrives). Every rank must make the same sequence of calls with the same
+ * sizes. */
+typedef struct cvsa_peer_desc {
+  const uint64_t* bases; /* device [world]: each rank's exchange buffer, mapped here */
+  int32_t world;         /* <= 8 */
+  int32_t rank;
+  int64_t row_cap;       /* floats per rank row the buffers were sized for */
+  int32_t* dev_error;    /* [1] CVSA_DEV_ERR_* bits, or NULL */
+} cvsa_peer_desc_t;
+
+/* Bytes of one rank's exchange buffer for rows of up to row_cap floats. */
+size_t cvsa_peer_buffer_bytes(int32_t world, int64_t row_cap);
+/* Allocate and zero an exchange buffer (cudaMalloc, set-up time) and write
+ * its CUDA IPC handle (64 bytes) to ipc_handle. */
+int cvsa_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+/* Map another rank's exchange buffer from its IPC handle. */
+int cvsa_peer_open(const void* ipc_handle, void** ptr);
+/* Unmap a buffer opened with cvsa_peer_open / free one from cvsa_peer_alloc. */
+int cvsa_peer_close(void* ptr);
+int cvsa_peer_free(void* ptr);
+/* out [world, n] = every rank's src [n] (floats, or any 32-bit words), rank order. */
+int cvsa_peer_allgather(const cvsa_peer_desc_t* pd, const float* src, int64_t n, float* out,
+                        void* stream);
+/* out [n] = element-wise minimum over the ranks of src [n] int32 (in place allowed). */
+int cvsa_peer_min_i32(const cvsa_peer_desc_t* pd, const int32_t* src, int64_t n, int32_t* out,
+                      void* stream);
+/* The page split's exchange of attention partials and their merge in one
+ * call: part = this rank's [o_unnorm (B·Hq·D) | m (B·Hq) | l (B·Hq)] row; out
+ * [B, Hq, D] (out_dtype) = the merge of every rank's row in rank order
+ * (cvsa_rank_merge's arithmetic), only heads with need != 0 when need
+ * ([B, H_kv] uint8) is given. */
+int cvsa_peer_merge(const cvsa_peer_desc_t* pd, const float* part, int32_t batch,
+                    int32_t num_kv_heads, int32_t num_q_per_kv, int32_t head_dim,
+                    const uint8_t* need, void* out, int32_t out_dtype, void* stream);
 
 /* Fused exact recovery: for heads with accept == 0, attend to the valid pages
  * NOT in the selection (skipped through a selection bitmap, never
