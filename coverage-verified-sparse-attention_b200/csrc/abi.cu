@@ -633,7 +633,7 @@ int cvsa_peer_allgather(const cvsa_peer_desc_t* pd, const float* src, int64_t n,
   if (n < 0 || n > pv.row_cap) return fail(CVSA_ERR_INVALID, "n outside [0, row_cap]");
   if (n == 0) return CVSA_OK;
   if (!src || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
-  if (n > (int64_t)peer_max_ctas() * 1024) return fail(CVSA_ERR_UNSUPPORTED, "row too long");
+  if (n > (int64_t)peer_max_ctas() * 256) return fail(CVSA_ERR_UNSUPPORTED, "row too long");
   return cuda_status(launch_peer_gather(pv, src, n, out, false, (cudaStream_t)stream),
                      "peer allgather launch");
 }
@@ -646,7 +646,7 @@ int cvsa_peer_min_i32(const cvsa_peer_desc_t* pd, const int32_t* src, int64_t n,
   if (n < 0 || n > pv.row_cap) return fail(CVSA_ERR_INVALID, "n outside [0, row_cap]");
   if (n == 0) return CVSA_OK;
   if (!src || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
-  if (n > (int64_t)peer_max_ctas() * 1024) return fail(CVSA_ERR_UNSUPPORTED, "row too long");
+  if (n > (int64_t)peer_max_ctas() * 256) return fail(CVSA_ERR_UNSUPPORTED, "row too long");
   return cuda_status(launch_peer_gather(pv, reinterpret_cast<const float*>(src), n,
                                         reinterpret_cast<float*>(out), true, (cudaStream_t)stream),
                      "peer min launch");
@@ -665,7 +665,8 @@ int cvsa_peer_merge(const cvsa_peer_desc_t* pd, const float* part, int32_t batch
   if (rows * (head_dim + 2) > pv.row_cap) return fail(CVSA_ERR_INVALID, "row_cap too small");
   if (rows == 0) return CVSA_OK;
   if (!part || !out) return fail(CVSA_ERR_INVALID, "NULL pointer");
-  if ((rows + 3) / 4 > peer_max_ctas()) return fail(CVSA_ERR_UNSUPPORTED, "too many query rows");
+  if (rows > peer_max_ctas()) return fail(CVSA_ERR_UNSUPPORTED, "too many query rows");
+  if (head_dim > 256) return fail(CVSA_ERR_UNSUPPORTED, "head_dim above 256");
   return cuda_status(launch_peer_merge(pv, part, batch, num_kv_heads, num_q_per_kv, head_dim,
                                        need, out, out_dtype, (cudaStream_t)stream),
                      "peer merge launch");

@@ -30,14 +30,14 @@
 namespace cvsa {
 namespace {
 
-constexpr int kPeerMaxCta = 128;
+constexpr int kPeerMaxCta = 65535;
 constexpr int kPeerMaxWorld = 8;
 constexpr size_t kPeerCallOff = 0;
 constexpr size_t kPeerDataOff = 8192;
 constexpr uint32_t kPeerSpinDefault = 0xffffffffu;  // no poll cap: the time cap applies
 constexpr int kGatherThreads = 256;
-constexpr int kGatherChunk = 1024;                // words per CTA
-constexpr int kMergeWarps = 4;                    // query rows per CTA
+constexpr int kGatherChunk = 256;                 // words per CTA
+constexpr int kMergeThreads = 128;                // one query row per CTA
 constexpr int kPeerMaxD = 256;                    // head_dim of the merge
 
 struct PeerArgs {
@@ -75,7 +75,10 @@ __device__ __forceinline__ void push_range(const PeerArgs& a, uint32_t slot, uin
   const int tid = threadIdx.x, nt = blockDim.x;
   const bool vec = ((lo | hi) & 1) == 0 && (reinterpret_cast<uintptr_t>(src) & 7) == 0 &&
                    (a.row_cap & 1) == 0;
-  for (int q = 0; q < a.world; ++q) {
+  // rank r starts with rank r + 1, so the ranks do not all write to the
+  // same GPU at once
+  for (int k = 1; k <= a.world; ++k) {
+    const int q = (a.rank + k) % a.world;
     uint2* dst = peer_row(a, q, slot, a.rank);
     if (vec) {
       for (int64_t i = lo + 2 * tid; i < hi; i += 2 * nt) {
@@ -202,73 +205,66 @@ peer_gather_kernel(const __grid_constant__ PeerArgs a, const uint32_t* __restric
 }
 
 // Exchange of attention partials and their merge: rank r's row is
-// [o (rows x D) | m (rows) | l (rows)] (rows = B * Hq). CTA c pushes and
-// merges query rows [c kMergeWarps, (c + 1) kMergeWarps) in rank order, as
-// cvsa_rank_merge does, and writes the normalised output (out dtype TO);
-// with `need`, only the rows of heads where need != 0.
+// [o (rows x D) | m (rows) | l (rows)] (rows = B * Hq). CTA `row` pushes and
+// merges that query row in rank order, as cvsa_rank_merge does, and writes
+// the normalised output (out dtype TO); with `need`, only the rows of heads
+// where need != 0 are written.
 template <typename TO>
-__global__ void __launch_bounds__(kMergeWarps * 32)
+__global__ void __launch_bounds__(kMergeThreads)
 peer_merge_kernel(const __grid_constant__ PeerArgs a, const float* __restrict__ part, int rows,
                   int hq, int G, int D, const uint8_t* __restrict__ need, TO* __restrict__ out) {
   __shared__ int s_fail;
-  __shared__ float s_o[kPeerMaxWorld][kMergeWarps][kPeerMaxD];
-  __shared__ float s_ml[kPeerMaxWorld][2][kMergeWarps];
+  __shared__ float s_o[kPeerMaxWorld][kPeerMaxD];
+  __shared__ float s_ml[kPeerMaxWorld][2];
   if (threadIdx.x == 0) s_fail = 0;
   const uint32_t e = call_number(a);
   const uint32_t slot = e & 1u;
-  const int r0 = blockIdx.x * kMergeWarps, nr = min(rows, r0 + kMergeWarps) - r0;
+  const int row = blockIdx.x;
   const int64_t m_off = (int64_t)rows * D, l_off = m_off + rows;
   const uint32_t* pw = reinterpret_cast<const uint32_t*>(part);
   __syncthreads();
-  push_range(a, slot, e, pw, (int64_t)r0 * D, (int64_t)(r0 + nr) * D);
-  push_range(a, slot, e, pw, m_off + r0, m_off + r0 + nr);
-  push_range(a, slot, e, pw, l_off + r0, l_off + r0 + nr);
-  // every rank's words of rows [r0, r0 + nr): o, then m and l
-  const int per = nr * (D + 2), od = nr * D;
+  push_range(a, slot, e, pw, (int64_t)row * D, (int64_t)(row + 1) * D);
+  if (threadIdx.x < a.world) {
+    // m and l of the row: two single words per rank
+    const int q = (a.rank + 1 + threadIdx.x) % a.world;
+    st_word(peer_row(a, q, slot, a.rank) + m_off + row, pw[m_off + row], e);
+    st_word(peer_row(a, q, slot, a.rank) + l_off + row, pw[l_off + row], e);
+  }
+  const int per = D + 2;
   fetch_words(
       a, slot, e, a.world * per,
       [&](int j, int& q, int64_t& i) {
         q = j / per;
         const int r = j - q * per;
-        if (r < od) {
-          i = (int64_t)r0 * D + r;
-        } else {
-          const int k = r - od;
-          i = (k < nr ? m_off : l_off - nr) + r0 + k;
-        }
+        i = r < D ? (int64_t)row * D + r : (r == D ? m_off : l_off) + row;
       },
       [&](int j, uint32_t w) {
         const int q = j / per, r = j - q * per;
-        if (r < od) {
-          s_o[q][r / D][r % D] = __uint_as_float(w);
-        } else {
-          const int k = r - od;
-          s_ml[q][k < nr ? 0 : 1][k < nr ? k : k - nr] = __uint_as_float(w);
-        }
+        if (r < D) s_o[q][r] = __uint_as_float(w);
+        else s_ml[q][r - D] = __uint_as_float(w);
       },
       &s_fail);
   __syncthreads();
-  const int wr = threadIdx.x >> 5, lane = threadIdx.x & 31, row = r0 + wr;
-  bool want = wr < nr;
-  if (want && need != nullptr) {
+  bool want = true;
+  if (need != nullptr) {
     const int b = row / hq;
     want = need[b * (hq / G) + (row % hq) / G] != 0;
   }
   if (want) {
     float M = neg_inf();
-    for (int q = 0; q < a.world; ++q) M = fmaxf(M, s_ml[q][0][wr]);
+    for (int q = 0; q < a.world; ++q) M = fmaxf(M, s_ml[q][0]);
     const float base = (M == neg_inf()) ? 0.f : M;
     float L = 0.f;
     for (int q = 0; q < a.world; ++q) {
-      const float mr = s_ml[q][0][wr];
-      if (mr != neg_inf()) L += s_ml[q][1][wr] * expf(mr - base);
+      const float mr = s_ml[q][0];
+      if (mr != neg_inf()) L += s_ml[q][1] * expf(mr - base);
     }
     const float denom = fmaxf(L, 1e-6f);
-    for (int d = lane; d < D; d += 32) {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
       float v = 0.f;
       for (int q = 0; q < a.world; ++q) {
-        const float mr = s_ml[q][0][wr];
-        if (mr != neg_inf()) v += s_o[q][wr][d] * expf(mr - base);
+        const float mr = s_ml[q][0];
+        if (mr != neg_inf()) v += s_o[q][d] * expf(mr - base);
       }
       out[(int64_t)row * D + d] = Elem<TO>::from_f(v / denom);
     }
@@ -317,21 +313,21 @@ cudaError_t launch_peer_merge(const PeerView& pv, const float* part, int B, int 
   if (rows <= 0) return cudaSuccess;
   if (!peer_shape_ok(pv) || (int64_t)rows * (D + 2) > pv.row_cap || D > kPeerMaxD)
     return cudaErrorInvalidValue;
-  const int ctas = (rows + kMergeWarps - 1) / kMergeWarps;
+  const int ctas = rows;
   if (ctas > kPeerMaxCta) return cudaErrorInvalidValue;
   const PeerArgs a = make_args(pv);
   const int hq = hkv * G;
   switch (out_dtype) {
     case CVSA_DTYPE_BF16:
-      peer_merge_kernel<<<ctas, kMergeWarps * 32, 0, s>>>(a, part, rows, hq, G, D, need,
+      peer_merge_kernel<<<ctas, kMergeThreads, 0, s>>>(a, part, rows, hq, G, D, need,
                                                           (__nv_bfloat16*)out);
       break;
     case CVSA_DTYPE_F16:
-      peer_merge_kernel<<<ctas, kMergeWarps * 32, 0, s>>>(a, part, rows, hq, G, D, need,
+      peer_merge_kernel<<<ctas, kMergeThreads, 0, s>>>(a, part, rows, hq, G, D, need,
                                                           (__half*)out);
       break;
     case CVSA_DTYPE_F32:
-      peer_merge_kernel<<<ctas, kMergeWarps * 32, 0, s>>>(a, part, rows, hq, G, D, need,
+      peer_merge_kernel<<<ctas, kMergeThreads, 0, s>>>(a, part, rows, hq, G, D, need,
                                                           (float*)out);
       break;
     default:

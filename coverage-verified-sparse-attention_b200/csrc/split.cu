@@ -31,10 +31,11 @@
 // selection: backend.py:446) and counts the step, so nothing reaches the
 // host and the step can be captured in a CUDA graph.
 //
-// Both kernels find the k-th largest candidate exactly with a 4-pass 8-bit
-// radix select on order-preserving keys (warp-aggregated shared histograms);
-// ties at the k-th key go to the lowest positions through a block prefix
-// count. Non-finite scores are never candidates.
+// Both kernels find the k-th largest candidate exactly on order-preserving
+// keys: a 2048-bin histogram of the top key bits, then a direct rank of the
+// keys in the bin holding it (radix passes over the low bits when that bin is
+// crowded); ties at the k-th key go to the lowest positions through a block
+// prefix count. Non-finite scores are never candidates.
 #include "cvsa_common.cuh"
 #include "cvsa_internal.h"
 #include "cvsa_launch.cuh"
@@ -104,16 +105,86 @@ __device__ __forceinline__ void block_lse(float& m, float& s, float* pm, float* 
 }
 
 // The k-th largest nonzero key of keys[0, n) (1 <= k <= number of nonzero
-// keys), by four 8-bit radix passes from the top byte. `above` returns the
-// number of keys strictly greater than the result.
+// keys). One pass histograms the top 11 key bits (2048 bins) and a block scan
+// finds the bin holding the k-th key; that bin's keys (usually a few dozen)
+// are gathered and each ranks itself against the others. A bin too full for
+// that (more than NT keys: heavy ties or a narrow score range) is resolved by
+// radix passes over the remaining 21 bits (8, 8 and 5). `above` returns the
+// number of keys strictly greater than the result. Scratch: hist[2048],
+// bin_keys[NT], sh[6], wsum (block_excl).
+constexpr int kTopBins = 2048;
+constexpr int kTopShift = 21;
+
 template <int NT>
-__device__ uint32_t block_kth_key(const uint32_t* keys, int n, int k, int* hist, int* sh,
-                                  int& above) {
+__device__ uint32_t block_kth_key(const uint32_t* keys, int n, int k, int* hist,
+                                  uint32_t* bin_keys, int* sh, int* wsum, int& above) {
+  constexpr int BPT = kTopBins / NT;  // bins per thread, highest first
   const int tid = threadIdx.x, lane = tid & 31;
-  uint32_t prefix = 0, mask = 0;
-  int abv = 0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += NT) hist[i] = 0;
+  for (int i = tid; i < kTopBins; i += NT) hist[i] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += NT) {
+    const uint32_t key = keys[i];
+    if (key != 0u) atomicAdd(&hist[key >> kTopShift], 1);
+  }
+  __syncthreads();
+  int c_sum = 0;
+#pragma unroll
+  for (int e = 0; e < BPT; ++e) c_sum += hist[kTopBins - 1 - (tid * BPT + e)];
+  int tot;
+  const int excl = block_excl<NT>(c_sum, wsum, tot);
+  if (excl < k && k <= excl + c_sum) {
+    int run = excl;
+#pragma unroll
+    for (int e = 0; e < BPT; ++e) {
+      const int bin = kTopBins - 1 - (tid * BPT + e);
+      const int c = hist[bin];
+      if (run < k && k <= run + c) {
+        sh[0] = bin;
+        sh[1] = run;
+        sh[2] = c;
+      }
+      run += c;
+    }
+  }
+  if (tid == 0) sh[3] = 0;
+  __syncthreads();
+  const uint32_t top = (uint32_t)sh[0];
+  int abv = sh[1];
+  const int cnt = sh[2];
+  if (cnt <= NT) {
+    for (int i = tid; i < n; i += NT) {
+      const uint32_t key = keys[i];
+      if (key != 0u && (key >> kTopShift) == top) bin_keys[atomicAdd(&sh[3], 1)] = key;
+    }
+    __syncthreads();
+    const int kk = k - abv;  // rank of the wanted key inside the bin, from 1
+    if (tid < cnt) {
+      const uint32_t my = bin_keys[tid];
+      int g = 0, eq = 0;
+      for (int j = 0; j < cnt; ++j) {
+        const uint32_t v = bin_keys[j];
+        g += v > my;
+        eq += v == my;
+      }
+      if (g < kk && kk <= g + eq) {  // every key equal to the answer agrees
+        sh[4] = (int)my;
+        sh[5] = abv + g;
+      }
+    }
+    __syncthreads();
+    above = sh[5];
+    const uint32_t T = (uint32_t)sh[4];
+    __syncthreads();
+    return T;
+  }
+  // radix passes over the low 21 bits of the keys in the bin
+  uint32_t prefix = top << kTopShift, mask = ~0u << kTopShift;
+#pragma unroll
+  for (int pass = 0; pass < 3; ++pass) {
+    const int shift = pass == 0 ? 13 : pass == 1 ? 5 : 0;
+    const int nb = pass == 2 ? 32 : 256, bpl = nb / 32;
+    const uint32_t dmask = (uint32_t)nb - 1u;
+    for (int i = tid; i < nb; i += NT) hist[i] = 0;
     __syncthreads();
     for (int i0 = 0; i0 < n; i0 += NT) {
       const int i = i0 + tid;
@@ -121,33 +192,33 @@ __device__ uint32_t block_kth_key(const uint32_t* keys, int n, int k, int* hist,
       const bool in = key != 0u && (key & mask) == prefix;
       const unsigned act = __ballot_sync(0xffffffffu, in);
       if (in) {
-        const uint32_t d = (key >> shift) & 255u;
+        const uint32_t d = (key >> shift) & dmask;
         const unsigned peers = __match_any_sync(act, d);
         if (lane == __ffs(peers) - 1) atomicAdd(&hist[d], __popc(peers));
       }
     }
     __syncthreads();
     if (tid < 32) {
-      // lane holds bins 255 - 8 lane - e (e = 0..7), highest digits first
-      int c[8], tot = 0;
+      // lane holds bins nb - 1 - bpl lane - e (e < bpl), highest digits first
+      int c[8], sum = 0;
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        c[e] = hist[255 - 8 * lane - e];
-        tot += c[e];
+        c[e] = e < bpl ? hist[nb - 1 - bpl * lane - e] : 0;
+        sum += c[e];
       }
-      int incl = tot;
+      int incl = sum;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      const int excl = incl - tot, need = k - abv;
-      if (excl < need && need <= incl) {
-        int run = excl;
+      const int ex = incl - sum, need = k - abv;
+      if (ex < need && need <= incl) {
+        int run = ex;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          if (run < need && need <= run + c[e]) {
-            sh[0] = 255 - 8 * lane - e;
+          if (e < bpl && run < need && need <= run + c[e]) {
+            sh[0] = nb - 1 - bpl * lane - e;
             sh[1] = run;
           }
           run += c[e];
@@ -156,7 +227,7 @@ __device__ uint32_t block_kth_key(const uint32_t* keys, int n, int k, int* hist,
     }
     __syncthreads();
     prefix |= (uint32_t)sh[0] << shift;
-    mask |= 255u << shift;
+    mask |= dmask << shift;
     abv += sh[1];
     __syncthreads();
   }
@@ -177,8 +248,9 @@ constexpr int kSplitSmemCap = 200 * 1024;  // dynamic shared memory of one CTA
 template <int NT>
 __global__ void __launch_bounds__(NT) split_propose_kernel(const __grid_constant__ SplitProposeParams p) {
   extern __shared__ uint32_t keys[];  // [W]
-  __shared__ int hist[256];
-  __shared__ int sh[2];
+  __shared__ int hist[kTopBins];
+  __shared__ uint32_t bin_keys[NT];
+  __shared__ int sh[6];
   __shared__ int wsum[NT / 32];
   __shared__ float pm[NT / 32], ps[NT / 32];
   pdl_wait();
@@ -213,7 +285,7 @@ __global__ void __launch_bounds__(NT) split_propose_kernel(const __grid_constant
   const int k = min(p.budget, cnt);
   uint32_t T = 0xffffffffu;
   int above = 0;
-  if (k > 0) T = block_kth_key<NT>(keys, W, k, hist, sh, above);
+  if (k > 0) T = block_kth_key<NT>(keys, W, k, hist, bin_keys, sh, wsum, above);
   const int take = k - above;  // ties at T, lowest pages first
   // contiguous pages per thread, so the compaction keeps page order
   const int per = (W + NT - 1) / NT;
@@ -267,8 +339,9 @@ __global__ void __launch_bounds__(NT) split_propose_kernel(const __grid_constant
 template <int NT>
 __global__ void __launch_bounds__(NT) split_gate_kernel(const __grid_constant__ SplitGateParams p) {
   extern __shared__ uint32_t smem[];  // keys [K] then the bitmap [bitmap_words]
-  __shared__ int hist[256];
-  __shared__ int sh[2];
+  __shared__ int hist[kTopBins];
+  __shared__ uint32_t bin_keys[NT];
+  __shared__ int sh[6];
   __shared__ int wsum[NT / 32];
   __shared__ float pm[NT / 32], ps[NT / 32];
   __shared__ float s_lse_all;
@@ -296,7 +369,7 @@ __global__ void __launch_bounds__(NT) split_gate_kernel(const __grid_constant__ 
   const int k = min(p.budget, cnt);
   uint32_t T = 0xffffffffu;
   int above = 0;
-  if (k > 0) T = block_kth_key<NT>(keys, K, k, hist, sh, above);
+  if (k > 0) T = block_kth_key<NT>(keys, K, k, hist, bin_keys, sh, wsum, above);
   const int take = k - above;
   const int per = (K + NT - 1) / NT;
   const int j0 = min(tid * per, K), j1 = min(j0 + per, K);
