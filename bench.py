@@ -1109,7 +1109,8 @@ def run_cvsa(args, ws, rank, local):
 
 
 KERNEL_CASES = ("select_warp", "select_big", "quest", "score_general", "attend_general",
-                "page_lse", "rank_merge", "append", "gather", "config3_step")
+                "page_lse", "rank_merge", "append", "gather", "config3_step", "split_propose",
+                "split_gate")
 
 
 def run_kernel_case(name: str, reps: int = 3):
@@ -1131,6 +1132,8 @@ def run_kernel_case(name: str, reps: int = 3):
         # fp32 pool: the general-layout kernels (score_pages_kernel, attend_kernel)
         wl = synthetic.small(device="cpu", seed=2, B=16, Hq=32, Hkv=8, D=128,
                              ctx=(8192,) * 16, dtype=torch.float32).to(dev)
+    elif name in ("split_propose", "split_gate"):
+        wl = None
     else:
         wl = synthetic.small(device="cpu", seed=2, B=8, Hq=32, Hkv=8, D=128,
                              ctx=(8192,) * 8).to(dev)
@@ -1144,6 +1147,32 @@ def run_kernel_case(name: str, reps: int = 3):
         for _ in range(reps + 1):
             be(wl.q, wl.k_cache, wl.v_cache, wl.block_tables, wl.context_lens, 0)
             be.step_done(0, 1)
+        torch.cuda.synchronize()
+        print(json.dumps({"kernel_case": name, "reps": reps}), flush=True)
+        return
+    if name in ("split_propose", "split_gate"):
+        # the page split's proposal over config 3 on one of 8 ranks (8 rows of
+        # 1024 pages) and its gate over the 8 ranks' gathered rows
+        from cvsa.kernels import split as SK
+        gen = torch.Generator().manual_seed(7)
+        H8, W8, budget8, max_sel8 = 8, 1024, 409, 412
+        lens8 = torch.full((1,), W8 * 16, dtype=torch.int32, device=dev)
+        rows8 = []
+        for r in range(8):
+            sc8 = torch.randn((1, H8, W8), generator=gen).to(dev)
+            row8 = torch.empty(SK.row_floats(1, H8, max_sel8), device=dev)
+            prop8 = SK.split_propose(sc8, lens8, 16, None, 1 if r == 0 else 0,
+                                     2 if r == 7 else 0, budget8, max_sel8, row8)
+            rows8.append(row8)
+        parts8 = torch.stack(rows8)
+        state8 = torch.zeros(4, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize()
+        for _ in range(reps):
+            if name == "split_propose":
+                SK.split_propose(sc8, lens8, 16, None, 0, 2, budget8, max_sel8, row8)
+            else:
+                SK.split_gate(parts8, prop8, lens8, 16, W8, 7, budget8, max_sel8, 0, 2, 0.9,
+                              False, 0, state8)
         torch.cuda.synchronize()
         print(json.dumps({"kernel_case": name, "reps": reps}), flush=True)
         return
