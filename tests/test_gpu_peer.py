@@ -152,3 +152,50 @@ def test_peer_two_gpus():
     mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world, join=True,
                        start_method="spawn")
     assert len(results) == world and all(results.values()), dict(results)
+
+
+def test_peer_wait_runs_out(cuda):
+    """A rank that never arrives: a two-rank exchange on one GPU whose second
+    rank's buffer is a plain local buffer nobody writes into this rank's. With
+    the wait limit cut to a few polls, every call returns and records
+    CVSA_DEV_ERR_TIMEOUT (no hang); the words that did land are still right;
+    with the limit restored a one-rank exchange on the same buffer runs clean."""
+    import ctypes
+    from cvsa import _lib
+    lib = _lib.load()
+    n = 300
+    nbytes = lib.cvsa_peer_buffer_bytes(2, n)
+    bufs = []
+    for _ in range(2):
+        p = ctypes.c_void_p()
+        h = ctypes.create_string_buffer(64)
+        _lib.check(lib.cvsa_peer_alloc(nbytes, ctypes.byref(p), h), "cvsa_peer_alloc")
+        bufs.append(p.value)
+    try:
+        bases = torch.tensor(bufs, dtype=torch.int64, device=cuda)
+        err = torch.zeros(1, dtype=torch.int32, device=cuda)
+        desc = _lib.PeerDesc(bases.data_ptr(), 2, 0, n, err.data_ptr())
+        x = torch.randn(n, device=cuda)
+        out = torch.full((2, n), 7.0, device=cuda)
+        lib.cvsa_set_wait_limit(64)
+        try:
+            _lib.check(lib.cvsa_peer_allgather(ctypes.byref(desc), x.data_ptr(), n,
+                                               out.data_ptr(), _lib.stream_ptr(cuda)),
+                       "cvsa_peer_allgather")
+            torch.cuda.synchronize()
+        finally:
+            lib.cvsa_set_wait_limit(0)
+        assert int(err.item()) & _lib.DEV_ERR_TIMEOUT
+        assert torch.equal(out[0], x)            # this rank's own row landed
+        # a clean one-rank exchange on the same buffer afterwards
+        err.zero_()
+        lib.cvsa_peer_free(ctypes.c_void_p(bufs.pop()))
+        one = _lib.PeerDesc(bases.data_ptr(), 1, 0, n, err.data_ptr())
+        out1 = torch.empty((1, n), device=cuda)
+        _lib.check(lib.cvsa_peer_allgather(ctypes.byref(one), x.data_ptr(), n, out1.data_ptr(),
+                                           _lib.stream_ptr(cuda)), "cvsa_peer_allgather")
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0 and torch.equal(out1[0], x)
+    finally:
+        for p in bufs:
+            lib.cvsa_peer_free(ctypes.c_void_p(p))
